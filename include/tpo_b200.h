@@ -1,0 +1,152 @@
+/*
+ * tpo_b200 -- C ABI of the B200-native chamfer / knn nearest-neighbour path.
+ *
+ * Plain pointers and sizes only; no torch types.  Every pointer argument is a
+ * DEVICE pointer on the current CUDA device unless stated otherwise, all point
+ * clouds are contiguous (B, P, D) arrays in the dtype given by `dtype`, and every
+ * call is asynchronous on `stream` (a cudaStream_t passed as void*; NULL = the
+ * legacy default stream).  Calls never abort the process: each returns a
+ * tpo_status (0 = success).  The library keeps no state between calls except
+ * per-device launch tuning, so calls are re-entrant.
+ *
+ * Each entry point names the reference function it replaces (paths relative to
+ * satyajitghana/torch-point-ops v0.1.0).
+ */
+#ifndef TPO_B200_H
+#define TPO_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TPO_API __attribute__((visibility("default")))
+#else
+#define TPO_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TPO_B200_ABI_VERSION 1
+
+/* element types (match torch's float32 / float16 / float64) */
+enum tpo_dtype { TPO_F32 = 0, TPO_F16 = 1, TPO_F64 = 2 };
+
+/* flags for the distance arithmetic.
+ * TPO_ROUND_FMA (default, 0): d = fma(dz,dz, fma(dy,dy, dx*dx)) -- the rounding of
+ *   the reference CUDA kernels (nvcc contracts chamfer.cu:67 and knn.cu:154).
+ * TPO_ROUND_EXACT: d = (dx*dx + dy*dy) + dz*dz with every operation rounded --
+ *   the rounding of the reference CPU path (knn.cpp:64-72).
+ * fp16 always rounds every operation (c10::Half semantics); the flag is ignored. */
+enum tpo_flags { TPO_ROUND_FMA = 0, TPO_ROUND_EXACT = 1 };
+
+enum tpo_status {
+  TPO_OK = 0,
+  TPO_ERR_INVALID_ARGUMENT = 1, /* bad shape / dtype / K / norm / null pointer   */
+  TPO_ERR_UNSUPPORTED = 2,      /* valid request this build does not implement  */
+  TPO_ERR_WORKSPACE = 3,        /* workspace missing or smaller than required   */
+  TPO_ERR_CUDA = 4,             /* a CUDA runtime call failed (see message)     */
+  TPO_ERR_DEVICE = 5            /* no usable sm_100 device                      */
+};
+
+/* Human-readable text for a status, including the last CUDA error text for
+ * TPO_ERR_CUDA on the calling thread. */
+TPO_API const char* tpo_status_string(int status);
+TPO_API int tpo_abi_version(void);
+
+/* ------------------------------------------------------------------------- */
+/* Chamfer distance forward.  Replaces chamfer_cuda_forward
+ * (torch_point_ops/chamfer/csrc/cuda/chamfer.cu:169-198) behind the
+ * torch_point_ops_chamfer::chamfer_forward schema (chamfer/csrc/chamfer.cpp:34-39).
+ *   xyz1 (B,N,3), xyz2 (B,M,3)                       dtype
+ *   dist1 (B,N), dist2 (B,M)                         dtype   (squared distance)
+ *   idx1 (B,N), idx2 (B,M)                           int32   (argmin, lowest index on ties)
+ * Both directions are produced from ONE evaluation of each (i,j) pair.
+ * Empty clouds give zeros, like the reference's torch::zeros outputs.
+ * `workspace` must hold tpo_chamfer_fwd_workspace_size() bytes (256-byte aligned);
+ * its contents on entry are ignored. */
+TPO_API size_t tpo_chamfer_fwd_workspace_size(int dtype, int64_t B, int64_t N, int64_t M);
+TPO_API int tpo_chamfer_fwd(int dtype, int flags, const void* xyz1, const void* xyz2, int64_t B,
+                    int64_t N, int64_t M, void* dist1, void* dist2, int32_t* idx1,
+                    int32_t* idx2, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Split form of tpo_chamfer_fwd for row-sharded multi-GPU runs (one rank owns rows
+ * [row_begin,row_end) of xyz1 and all of xyz2).  Keys are packed (distance bits,
+ * candidate-chunk) words; their minimum over ranks is the global answer, so an
+ * element-wise MIN all-reduce of keys2 (as int64 for f32/f16) merges ranks.
+ *   key bytes per point: tpo_chamfer_key_bytes(dtype) (8 for f32/f16, 16 for f64)
+ *   keys_init:  set n keys to the empty value.
+ *   fwd_keys:   fold pairs (rows [row_begin,row_end) x all M) into keys1/keys2.
+ *   finalize:   turn keys into (dist, idx) for rows [row_begin,row_end) of cloud 1
+ *               (dist1/idx1 point at row 0 of each batch as usual) and for all of
+ *               cloud 2 when dist2 != NULL. */
+TPO_API int tpo_chamfer_key_bytes(int dtype);
+TPO_API int tpo_chamfer_keys_init(int dtype, void* keys, int64_t n, void* stream);
+TPO_API int tpo_chamfer_fwd_keys(int dtype, int flags, const void* xyz1, const void* xyz2, int64_t B,
+                         int64_t N, int64_t M, int64_t row_begin, int64_t row_end,
+                         void* keys1, void* keys2, void* stream);
+TPO_API int tpo_chamfer_finalize(int dtype, int flags, const void* xyz1, const void* xyz2, int64_t B,
+                         int64_t N, int64_t M, int64_t row_begin, int64_t row_end,
+                         const void* keys1, const void* keys2, void* dist1, int32_t* idx1,
+                         void* dist2, int32_t* idx2, void* stream);
+
+/* Chamfer distance backward.  Replaces chamfer_cuda_backward (chamfer.cu:236-271):
+ *   grad_xyz1[i]      += 2*g1[i]*(xyz1[i] - xyz2[idx1[i]])
+ *   grad_xyz2[idx1[i]] -= the same, and symmetrically for direction 2.
+ * grad_xyz1 / grad_xyz2 are fully written (no need to zero them).
+ * Either grad_dist pointer may be NULL (treated as zeros). */
+TPO_API int tpo_chamfer_bwd(int dtype, const void* xyz1, const void* xyz2, int64_t B, int64_t N,
+                    int64_t M, const int32_t* idx1, const int32_t* idx2,
+                    const void* grad_dist1, const void* grad_dist2, void* grad_xyz1,
+                    void* grad_xyz2, void* stream);
+/* Row-sharded backward: only rows [row_begin,row_end) of cloud 1 and columns
+ * [col_begin,col_end) of cloud 2 contribute; grads are ACCUMULATED (caller zeroes
+ * them) so that a SUM all-reduce over ranks gives the full gradient. */
+TPO_API int tpo_chamfer_bwd_partial(int dtype, const void* xyz1, const void* xyz2, int64_t B,
+                            int64_t N, int64_t M, int64_t row_begin, int64_t row_end,
+                            int64_t col_begin, int64_t col_end, const int32_t* idx1,
+                            const int32_t* idx2, const void* grad_dist1,
+                            const void* grad_dist2, void* grad_xyz1, void* grad_xyz2,
+                            void* stream);
+
+/* ------------------------------------------------------------------------- */
+/* K nearest neighbours forward.  Replaces knn_cuda_forward
+ * (torch_point_ops/knn/csrc/cuda/knn.cu:295-398) behind
+ * torch_point_ops_knn::knn_forward (knn/csrc/knn.cpp:167-169), with the sort of
+ * knn_points (knn/__init__.py:110-131) done in the kernel:
+ *   p1 (N,P1,D), p2 (N,P2,D) dtype; lengths1/lengths2 (N,) int64 (NULL = full)
+ *   dists (N,P1,K) dtype, idxs (N,P1,K) int64
+ * For each valid query (p < lengths1[n]) the K smallest (dist, idx) pairs over
+ * the first lengths2[n] points, ascending by (dist, idx).  Slots k >= lengths2[n]
+ * and rows p >= lengths1[n] hold idx -1 / dist 0 (the reference CPU padding,
+ * knn.cpp:44-45).  norm: 2 = squared L2, 1 = L1.  1 <= K <= 32, 1 <= D <= 8. */
+TPO_API int tpo_knn_fwd(int dtype, int flags, const void* p1, const void* p2,
+                const int64_t* lengths1, const int64_t* lengths2, int64_t N, int64_t P1,
+                int64_t P2, int64_t D, int64_t norm, int64_t K, void* dists, int64_t* idxs,
+                void* stream);
+
+/* knn backward.  Replaces knn_cuda_backward (knn.cu:469-534):
+ *   L2: v = 2*g*(p1-p2); L1: v = g*sign(p1-p2) (0 at equality, knn.cu:447-449)
+ *   grad_p1[row] += v; grad_p2[idx] -= v; rows >= lengths1 and idx -1 skipped.
+ * grad_p1 / grad_p2 are fully written. */
+TPO_API int tpo_knn_bwd(int dtype, const void* p1, const void* p2, const int64_t* lengths1,
+                const int64_t* lengths2, const int64_t* idxs, int64_t N, int64_t P1,
+                int64_t P2, int64_t D, int64_t K, int64_t norm, const void* grad_dists,
+                void* grad_p1, void* grad_p2, void* stream);
+
+/* knn_gather forward (knn/__init__.py:136-183): out[n,l,k,:] = x[n, idx[n,l,k], :],
+ * zero where k >= lengths[n] or idx == -1.  x (N,M,U), idx (N,L,K) int64,
+ * lengths (N,) int64 or NULL, out (N,L,K,U). */
+TPO_API int tpo_knn_gather_fwd(int dtype, const void* x, const int64_t* idx, const int64_t* lengths,
+                       int64_t N, int64_t M, int64_t U, int64_t L, int64_t K, void* out,
+                       void* stream);
+/* Its backward: grad_x (N,M,U) fully written with the scatter-add of grad_out. */
+TPO_API int tpo_knn_gather_bwd(int dtype, const void* grad_out, const int64_t* idx,
+                       const int64_t* lengths, int64_t N, int64_t M, int64_t U, int64_t L,
+                       int64_t K, void* grad_x, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TPO_B200_H */

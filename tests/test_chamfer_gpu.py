@@ -1,0 +1,187 @@
+"""Chamfer parity on the B200: the CUDA path (through the C ABI and through the
+torch API) against the CPU oracle on the same seeded inputs.
+Indices bit-exact; distances bit-exact (same rounding as the selected mode);
+gradients within 1e-6 (fp32) / 1e-12 (fp64) / 1e-3 (fp16) of the summed term
+magnitude (the reference itself scatters with atomics, so summation order is free)."""
+import numpy as np
+import pytest
+import torch
+
+import capi_util as C
+import datagen
+import oracle
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+RTOL = {torch.float32: 1e-6, torch.float64: 1e-12, torch.float16: 1e-3}
+
+
+def _bits(t):
+    a = t.detach().cpu().contiguous().numpy()
+    return a.view(np.uint8)
+
+
+def _check_fwd(x1, x2, flags=0):
+    mode = 1 if flags == 0 else 0
+    d1, d2, i1, i2 = C.chamfer_fwd(x1.to(DEV), x2.to(DEV), flags)
+    torch.cuda.synchronize()
+    od1, od2, oi1, oi2 = oracle.chamfer_fwd(x1.numpy(), x2.numpy(), mode)
+    assert np.array_equal(i1.cpu().numpy(), oi1), "idx1 mismatch"
+    assert np.array_equal(i2.cpu().numpy(), oi2), "idx2 mismatch"
+    assert np.array_equal(_bits(d1), od1.view(np.uint8)), "dist1 bits"
+    assert np.array_equal(_bits(d2), od2.view(np.uint8)), "dist2 bits"
+    return d1, d2, i1, i2
+
+
+def _term_scale(x1, x2, i1, i2, g1, g2):
+    """Per-element sum of |terms| entering each gradient element (float64)."""
+    a, b = x1.double().numpy(), x2.double().numpy()
+    i1, i2 = i1.cpu().numpy().astype(np.int64), i2.cpu().numpy().astype(np.int64)
+    s1 = np.zeros_like(a)
+    s2 = np.zeros_like(b)
+    for bi in range(a.shape[0]):
+        t = np.abs(2 * g1[bi].double().numpy()[:, None] * (a[bi] - b[bi][i1[bi]]))
+        s1[bi] += t
+        np.add.at(s2[bi], i1[bi], t)
+        t = np.abs(2 * g2[bi].double().numpy()[:, None] * (b[bi] - a[bi][i2[bi]]))
+        s2[bi] += t
+        np.add.at(s1[bi], i2[bi], t)
+    return s1, s2
+
+
+def _check_bwd(x1, x2, i1, i2, seed=0):
+    B, N, _ = x1.shape
+    M = x2.shape[1]
+    g = torch.Generator().manual_seed(seed)
+    g1 = torch.randn(B, N, generator=g).to(x1.dtype)
+    g2 = torch.randn(B, M, generator=g).to(x1.dtype)
+    gx1, gx2 = C.chamfer_bwd(x1.to(DEV), x2.to(DEV), i1, i2, g1.to(DEV), g2.to(DEV))
+    torch.cuda.synchronize()
+    o1, o2 = oracle.chamfer_bwd(x1.numpy(), x2.numpy(), i1.cpu().numpy(), i2.cpu().numpy(),
+                                g1.numpy(), g2.numpy())
+    s1, s2 = _term_scale(x1, x2, i1, i2, g1, g2)
+    tol = RTOL[x1.dtype]
+    e1 = np.abs(gx1.cpu().double().numpy() - o1.astype(np.float64))
+    e2 = np.abs(gx2.cpu().double().numpy() - o2.astype(np.float64))
+    tiny = np.finfo(np.float16).tiny if x1.dtype == torch.float16 else 0
+    assert np.all(e1 <= tol * s1 + tiny), float(np.max(e1 - tol * s1))
+    assert np.all(e2 <= tol * s2 + tiny), float(np.max(e2 - tol * s2))
+
+
+SIZES = [(1, 1, 1), (1, 3, 4), (2, 5, 7), (1, 8, 6), (2, 64, 128), (2, 511, 513), (3, 1000, 1500),
+         (1, 2048, 64), (1, 64, 2048), (4, 1024, 1024), (1, 2049, 777)]
+
+
+@pytest.mark.parametrize("B,N,M", SIZES)
+@pytest.mark.parametrize("flags", [0, 1])
+def test_fwd_bwd_f32_uniform(B, N, M, flags):
+    x1 = datagen.uniform(B, N, seed=N * 31 + M)
+    x2 = datagen.uniform(B, M, seed=N * 17 + M + 1)
+    d1, d2, i1, i2 = _check_fwd(x1, x2, flags)
+    _check_bwd(x1, x2, i1, i2)
+
+
+@pytest.mark.parametrize("dtype", [torch.float64, torch.float16])
+@pytest.mark.parametrize("B,N,M", [(1, 3, 4), (2, 300, 517), (3, 1000, 1500), (1, 2049, 777)])
+def test_fwd_bwd_f64_f16(dtype, B, N, M):
+    x1 = datagen.sphere_noise(B, N, seed=N, dtype=dtype)
+    x2 = datagen.sphere_noise(B, M, seed=M + 7, dtype=dtype)
+    d1, d2, i1, i2 = _check_fwd(x1, x2, 0)
+    _check_bwd(x1, x2, i1, i2)
+    if dtype == torch.float64:
+        _check_fwd(x1, x2, 1)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float64, torch.float16])
+def test_ties_lowest_index(dtype):
+    # integer grid points: many exactly equal distances; duplicates in both clouds
+    g = torch.Generator().manual_seed(11)
+    x1 = torch.randint(0, 5, (2, 700, 3), generator=g).to(dtype)
+    x2 = torch.randint(0, 5, (2, 900, 3), generator=g).to(dtype)
+    _check_fwd(x1, x2, 0)
+    _check_fwd(x1, x2, 1)
+
+
+def test_known_values():
+    a = torch.zeros(1, 1, 3, device=DEV)
+    b = torch.tensor([[[1.0, 2.0, 3.0]]], device=DEV)
+    d1, d2, i1, i2 = C.chamfer_fwd(a, b)
+    assert d1.item() == 14 and d2.item() == 14
+    x = torch.rand(2, 100, 3, device=DEV)
+    d1, d2, i1, i2 = C.chamfer_fwd(x, x)
+    assert torch.all(d1 == 0) and torch.all(d2 == 0)
+
+
+@pytest.mark.parametrize("N,M", [(0, 5), (5, 0), (0, 0)])
+def test_empty_clouds(N, M):
+    x1 = torch.rand(2, N, 3, device=DEV)
+    x2 = torch.rand(2, M, 3, device=DEV)
+    d1, d2, i1, i2 = C.chamfer_fwd(x1, x2)
+    assert d1.shape == (2, N) and d2.shape == (2, M)
+    assert torch.all(d1 == 0) and torch.all(i1 == 0) and torch.all(d2 == 0)
+
+
+def test_config2_full_size_f32_and_f16():
+    for dtype in (torch.float32, torch.float16):
+        x1 = datagen.sphere_noise(32, 2048, seed=20, dtype=dtype)
+        x2 = datagen.sphere_noise(32, 2048, seed=21, dtype=dtype)
+        _, _, i1, i2 = _check_fwd(x1, x2, 0)
+        _check_bwd(x1, x2, i1, i2)
+
+
+def test_config3_full_size():
+    x1 = datagen.gmm(16, 16384, seed=30)
+    x2 = datagen.gmm(16, 8192, seed=31)
+    _check_fwd(x1, x2, 0)
+
+
+def test_config5_sampled_rows_f32():
+    """1M x 1M: full GPU run, oracle on sampled rows/columns (size-independent check)."""
+    N = 1 << 20
+    x1 = datagen.lidar(N, seed=50)
+    x2 = datagen.lidar(N, seed=51)
+    d1, d2, i1, i2 = C.chamfer_fwd(x1.to(DEV), x2.to(DEV))
+    torch.cuda.synchronize()
+    g = torch.Generator().manual_seed(0)
+    rows = torch.randint(0, N, (2048,), generator=g)
+    od, oi = oracle.nn(x1[:, rows].numpy(), x2.numpy(), 1)
+    assert np.array_equal(i1[:, rows].cpu().numpy(), oi)
+    assert np.array_equal(_bits(d1[:, rows]), od.view(np.uint8))
+    od, oi = oracle.nn(x2[:, rows].numpy(), x1.numpy(), 1)
+    assert np.array_equal(i2[:, rows].cpu().numpy(), oi)
+    # properties over every point: dist1[i] == |x1[i] - x2[idx1[i]]|^2 recomputed
+    a, b = x1[0].to(DEV), x2[0].to(DEV)
+    r = ((b[i1[0].long()] - a) ** 2)
+    assert torch.all(d1[0] <= r.sum(-1) * (1 + 1e-6) + 1e-30)
+
+
+def test_torch_api_autograd_matches_capi():
+    import torch_point_ops_b200 as tpo
+
+    x1 = datagen.uniform(3, 700, seed=1).to(DEV).requires_grad_()
+    x2 = datagen.uniform(3, 500, seed=2).to(DEV).requires_grad_()
+    loss = tpo.ChamferDistance("mean")(x1, x2)
+    loss.backward()
+    d1, d2, i1, i2 = C.chamfer_fwd(x1.detach(), x2.detach())
+    ref = d1.mean() + d2.mean()
+    assert torch.allclose(loss.detach(), ref, rtol=1e-6)
+    g1 = torch.full_like(d1, 1.0 / d1.numel())
+    g2 = torch.full_like(d2, 1.0 / d2.numel())
+    gx1, gx2 = C.chamfer_bwd(x1.detach(), x2.detach(), i1, i2, g1, g2)
+    assert torch.allclose(x1.grad, gx1, rtol=1e-5, atol=1e-9)
+    assert torch.allclose(x2.grad, gx2, rtol=1e-5, atol=1e-9)
+    for red in ("sum", None, "none"):
+        out = tpo.ChamferDistance(red)(x1, x2)
+    assert isinstance(out, tuple) and out[0].shape == (3, 700)
+    with pytest.raises(ValueError):
+        tpo.ChamferDistance("max")
+
+
+def test_gradcheck_f64():
+    import torch_point_ops_b200 as tpo
+
+    g = torch.Generator().manual_seed(5)
+    x1 = torch.rand(1, 8, 3, generator=g, dtype=torch.float64).to(DEV).requires_grad_()
+    x2 = torch.rand(1, 6, 3, generator=g, dtype=torch.float64).to(DEV).requires_grad_()
+    assert torch.autograd.gradcheck(lambda a, b: tpo.chamfer_distance(a, b), (x1, x2),
+                                    nondet_tol=1e-12)

@@ -1,0 +1,59 @@
+"""Pins the rounding of the reference's own CUDA kernels on the B200.
+
+oracle/_ref holds the reference chamfer/knn sources compiled unmodified with the
+flags of the reference's setup.py (oracle/Makefile.ref).  On the GPU this checks
+that (a) the reference CUDA distances equal the oracle's "fma" mode bit for bit
+-- i.e. nvcc contracts dx*dx+dy*dy+dz*dz into fma(dz,dz,fma(dy,dy,dx*dx)) --
+and (b) this library's default output equals the reference CUDA output.
+Skipped when oracle/_ref was not built."""
+import numpy as np
+import pytest
+import torch
+
+import capi_util as C
+import datagen
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+def _bits(t):
+    return t.detach().cpu().contiguous().numpy().view(np.uint8)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float64, torch.float16])
+def test_reference_chamfer_cuda_rounding(dtype):
+    ops = oracle.ref_chamfer()
+    if ops is None:
+        pytest.skip("reference CUDA build not present in oracle/_ref")
+    x1 = datagen.sphere_noise(4, 1500, seed=1, dtype=dtype)
+    x2 = datagen.sphere_noise(4, 1300, seed=2, dtype=dtype)
+    rd1, rd2, ri1, ri2 = ops.chamfer_forward(x1.cuda(), x2.cuda())
+    od1, od2, oi1, oi2 = oracle.chamfer_fwd(x1.numpy(), x2.numpy(), 1)
+    assert np.array_equal(_bits(rd1), od1.view(np.uint8)), "reference CUDA rounding != fma mode"
+    assert np.array_equal(ri1.cpu().numpy(), oi1)
+    assert np.array_equal(ri2.cpu().numpy(), oi2)
+    d1, d2, i1, i2 = C.chamfer_fwd(x1.cuda(), x2.cuda(), 0)
+    assert torch.equal(i1.cpu(), ri1.cpu()) and torch.equal(i2.cpu(), ri2.cpu())
+    assert np.array_equal(_bits(d1), _bits(rd1)) and np.array_equal(_bits(d2), _bits(rd2))
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float64])
+def test_reference_knn_cuda_rounding(dtype):
+    ops = oracle.ref_knn()
+    if ops is None or not oracle._ref_loaded.get("knn_cuda_ref.so"):
+        pytest.skip("reference CUDA knn build not present in oracle/_ref")
+    g = torch.Generator().manual_seed(3)
+    p1 = torch.randn(2, 500, 3, generator=g).to(dtype)
+    p2 = torch.randn(2, 700, 3, generator=g).to(dtype)
+    L1 = torch.full((2,), 500)
+    L2 = torch.full((2,), 700)
+    ri, rd = ops.knn_forward(p1.cuda(), p2.cuda(), L1.cuda(), L2.cuda(), 2, 16, -1)
+    # the reference sorts in Python (knn/__init__.py:130-131)
+    rd, order = rd.sort(dim=2)
+    ri = ri.gather(2, order)
+    oi, od = oracle.knn_fwd(p1.numpy(), p2.numpy(), L1.numpy(), L2.numpy(), 2, 16, 1)
+    assert np.array_equal(_bits(rd), od.view(np.uint8))
+    assert np.array_equal(ri.cpu().numpy(), oi)
+    i, d = C.knn_fwd(p1.cuda(), p2.cuda(), L1.cuda(), L2.cuda(), 2, 16, 0)
+    assert torch.equal(i.cpu(), ri.cpu())

@@ -1,0 +1,119 @@
+// Chamfer backward: gradient scatter through the argmin indices.
+//
+// Replaces chamfer_dist_grad_kernel (torch_point_ops/chamfer/csrc/cuda/
+// chamfer.cu:200-234), which is launched twice on 16 CTAs.  Here both directions
+// run in ONE grid-stride launch sized to the whole GPU; each point gathers its
+// nearest neighbour, forms v = (2*grad) * (p - nn) with the reference's
+// per-operation rounding (g = grad*2, :222; g*(x1-x2), :226-231), adds v to its
+// own gradient and subtracts it from its neighbour's with fire-and-forget
+// atomics.  HBM-bound: per point it reads its coordinates, index and grad, the
+// neighbour's coordinates, and issues 6 reductions.
+#include "tpo_internal.h"
+
+namespace tpo {
+
+template <typename T>
+struct BwdOps;
+template <>
+struct BwdOps<float> {
+  __device__ static float two_g(float g) { return __fmul_rn(g, 2.0f); }
+  __device__ static float term(float g2, float a, float b) { return __fmul_rn(g2, __fsub_rn(a, b)); }
+  __device__ static void add(float* p, float v) { atomicAdd(p, v); }
+  __device__ static float neg(float v) { return -v; }
+};
+template <>
+struct BwdOps<double> {
+  __device__ static double two_g(double g) { return __dmul_rn(g, 2.0); }
+  __device__ static double term(double g2, double a, double b) { return __dmul_rn(g2, __dsub_rn(a, b)); }
+  __device__ static void add(double* p, double v) { atomicAdd(p, v); }
+  __device__ static double neg(double v) { return -v; }
+};
+template <>
+struct BwdOps<__half> {
+  __device__ static __half two_g(__half g) { return hmul_rn(g, __float2half_rn(2.0f)); }
+  __device__ static __half term(__half g2, __half a, __half b) { return hmul_rn(g2, hsub_rn(a, b)); }
+  __device__ static void add(__half* p, __half v) { atomicAdd(p, v); }
+  __device__ static __half neg(__half v) { return __hneg(v); }
+};
+
+template <typename T>
+__global__ void chamfer_bwd_kernel(const T* __restrict__ x1, const T* __restrict__ x2, int64_t B,
+                                   int64_t N, int64_t M, int64_t r0, int64_t r1, int64_t c0,
+                                   int64_t c1, const int32_t* __restrict__ i1,
+                                   const int32_t* __restrict__ i2, const T* __restrict__ g1,
+                                   const T* __restrict__ g2, T* __restrict__ gx1,
+                                   T* __restrict__ gx2) {
+  using O = BwdOps<T>;
+  const int64_t nr = (g1 && M > 0) ? r1 - r0 : 0;
+  const int64_t nc = (g2 && N > 0) ? c1 - c0 : 0;
+  const int64_t n1 = B * nr;
+  const int64_t total = n1 + B * nc;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const T *pa, *pb;
+    T *ga, *gb;
+    T g;
+    if (t < n1) {
+      const int64_t b = t / nr, i = r0 + t % nr;
+      const int64_t o = b * N + i;
+      const int64_t j = i1[o];
+      pa = x1 + o * 3;
+      pb = x2 + (b * M + j) * 3;
+      ga = gx1 + o * 3;
+      gb = gx2 + (b * M + j) * 3;
+      g = g1[o];
+    } else {
+      const int64_t u = t - n1;
+      const int64_t b = u / nc, j = c0 + u % nc;
+      const int64_t o = b * M + j;
+      const int64_t i = i2[o];
+      pa = x2 + o * 3;
+      pb = x1 + (b * N + i) * 3;
+      ga = gx2 + o * 3;
+      gb = gx1 + (b * N + i) * 3;
+      g = g2[o];
+    }
+    const T gg = O::two_g(g);
+#pragma unroll
+    for (int d = 0; d < 3; ++d) {
+      const T v = O::term(gg, pa[d], pb[d]);
+      O::add(ga + d, v);
+      O::add(gb + d, O::neg(v));
+    }
+  }
+}
+
+template <typename T>
+static int launch_bwd(const T* x1, const T* x2, int64_t B, int64_t N, int64_t M, int64_t r0,
+                      int64_t r1, int64_t c0, int64_t c1, const int32_t* i1, const int32_t* i2,
+                      const T* g1, const T* g2, T* gx1, T* gx2, cudaStream_t st) {
+  const int64_t total = B * ((g1 && M > 0) ? r1 - r0 : 0) + B * ((g2 && N > 0) ? c1 - c0 : 0);
+  if (total <= 0) return TPO_OK;
+  const int threads = 256;
+  const int64_t blocks = std::min<int64_t>((total + threads - 1) / threads, 148 * 16);
+  chamfer_bwd_kernel<T><<<(unsigned)blocks, threads, 0, st>>>(x1, x2, B, N, M, r0, r1, c0, c1, i1,
+                                                               i2, g1, g2, gx1, gx2);
+  return check_launch();
+}
+
+int chamfer_bwd_accumulate(int dtype, const void* x1, const void* x2, int64_t B, int64_t N,
+                           int64_t M, int64_t r0, int64_t r1, int64_t c0, int64_t c1,
+                           const int32_t* i1, const int32_t* i2, const void* g1, const void* g2,
+                           void* gx1, void* gx2, cudaStream_t st) {
+  switch (dtype) {
+    case TPO_F32:
+      return launch_bwd<float>((const float*)x1, (const float*)x2, B, N, M, r0, r1, c0, c1, i1, i2,
+                               (const float*)g1, (const float*)g2, (float*)gx1, (float*)gx2, st);
+    case TPO_F16:
+      return launch_bwd<__half>((const __half*)x1, (const __half*)x2, B, N, M, r0, r1, c0, c1, i1,
+                                i2, (const __half*)g1, (const __half*)g2, (__half*)gx1,
+                                (__half*)gx2, st);
+    case TPO_F64:
+      return launch_bwd<double>((const double*)x1, (const double*)x2, B, N, M, r0, r1, c0, c1, i1,
+                                i2, (const double*)g1, (const double*)g2, (double*)gx1,
+                                (double*)gx2, st);
+  }
+  return TPO_ERR_INVALID_ARGUMENT;
+}
+
+}  // namespace tpo

@@ -1,0 +1,584 @@
+// Chamfer forward: fused bidirectional nearest neighbour for sm_100a.
+//
+// Replaces the reference's chamfer_dist_kernel (torch_point_ops/chamfer/csrc/
+// cuda/chamfer.cu:37-167), which runs the full (B,N,M) distance matrix twice,
+// once per direction.  Here every (i,j) pair is evaluated ONCE and feeds both
+// the row minimum (dist1/idx1) and the column minimum (dist2/idx2).
+//
+// Work decomposition.  A CTA takes a unit = (batch, row block, column segment).
+// Each warp owns 32 lanes x R consecutive rows held in registers; the CTA's
+// warps share the column segment, staged 256 columns at a time into shared
+// memory (coordinates duplicated into {c,c} pairs so one packed fp32x2 op
+// serves two rows).  A step processes 4 columns against the lane's R rows:
+//   * row side   : running min per row (3-input FMNMX) + the 4-column chunk in
+//                  which it last strictly improved (strict '<' in increasing
+//                  column order => lowest column on ties);
+//   * column side: min over the lane's R rows, then a warp-wide redux.min on
+//                  the (non-negative float) bit pattern and a ballot for the
+//                  lowest lane holding it (=> lowest row chunk on ties).
+// Partial results are packed keys  (distance bits << 32) | chunk start  and
+// merged across warps (shared memory) and CTAs (global atomic min).  Because the
+// distance is >= 0 its bit pattern orders like the value, so the key order is
+// (distance, index) -- exactly the reference's tie rule (chamfer.cu:69 strict
+// '<' inside a tile, :159 strict '>' across tiles => lowest index wins).
+// A finalize pass decodes each key and rescans its chunk (4 columns or R rows)
+// with the identical arithmetic to recover the exact index.
+//
+// fp32 runs on packed fp32x2 instructions; fp16 computes the c10::Half
+// per-operation-rounded distance and runs the same float machinery on its exact
+// float value; fp64 uses 128-bit keys merged by a 16-byte compare-and-swap.
+#include "tpo_internal.h"
+
+namespace tpo {
+
+// ----------------------------- fp32 fast path -----------------------------
+constexpr int CF_R = 16;              // rows per lane
+constexpr int CF_RP = CF_R / 2;       // packed row pairs per lane
+constexpr int CF_C = 4;               // columns per step (= row-side chunk)
+constexpr int CF_TILE_STEPS = 64;     // steps per shared-memory tile
+constexpr int CF_TILE = CF_TILE_STEPS * CF_C;
+constexpr int CF_MAXW = 4;            // warps per CTA
+constexpr int CF_ROWS_PER_WARP = 32 * CF_R;
+
+template <int MODE>
+__global__ void __launch_bounds__(CF_MAXW * 32)
+    chamfer_keys_f32_kernel(const float* __restrict__ xyz1, const float* __restrict__ xyz2,
+                            int64_t N, int64_t M, int64_t row_begin, int64_t row_end,
+                            int rb_count, int cs_count, int64_t seg,
+                            u64* __restrict__ keys1, u64* __restrict__ keys2) {
+  __shared__ __align__(16) float2 s_col[CF_TILE_STEPS][3][CF_C];
+  __shared__ __align__(16) u64 s_key[CF_MAXW][CF_TILE];
+
+  const int W = blockDim.x >> 5;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  int64_t unit = blockIdx.x;
+  const int cs = (int)(unit % cs_count);
+  unit /= cs_count;
+  const int rb = (int)(unit % rb_count);
+  const int64_t b = unit / rb_count;
+  const int64_t c0 = (int64_t)cs * seg;
+  const int64_t c1 = min(M, c0 + seg);
+  const int64_t blk_row0 = row_begin + (int64_t)rb * W * CF_ROWS_PER_WARP;
+  const int64_t warp_row0 = blk_row0 + (int64_t)warp * CF_ROWS_PER_WARP;
+  const int64_t lane_row0 = warp_row0 + (int64_t)lane * CF_R;
+  const bool warp_active = warp_row0 < row_end;
+  const int n_active = (int)min64(W, (row_end - blk_row0 + CF_ROWS_PER_WARP - 1) / CF_ROWS_PER_WARP);
+  const float qnan = __int_as_float(0x7fffffff);
+
+  u64 QX[CF_RP], QY[CF_RP], QZ[CF_RP];
+  {
+    const float* a = xyz1 + (b * N + lane_row0) * 3;
+#pragma unroll
+    for (int p = 0; p < CF_RP; ++p) {
+      float v[6];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const bool ok = lane_row0 + 2 * p + h < row_end;
+#pragma unroll
+        for (int d = 0; d < 3; ++d) v[h * 3 + d] = ok ? __ldg(a + (2 * p + h) * 3 + d) : qnan;
+      }
+      QX[p] = pk(v[0], v[3]);
+      QY[p] = pk(v[1], v[4]);
+      QZ[p] = pk(v[2], v[5]);
+    }
+  }
+  float best[CF_R];
+  int bchunk[CF_R];
+#pragma unroll
+  for (int r = 0; r < CF_R; ++r) {
+    best[r] = __int_as_float(0x7f800000);
+    bchunk[r] = 0;
+  }
+
+  for (int64_t tc = c0; tc < c1; tc += CF_TILE) {
+    const int ncols = (int)min64(CF_TILE, c1 - tc);
+    const int nsteps = (ncols + CF_C - 1) / CF_C;
+    __syncthreads();
+    {
+      const float* src = xyz2 + (b * M + tc) * 3;
+      float* dst = reinterpret_cast<float*>(&s_col[0][0][0]);
+      for (int e = threadIdx.x; e < nsteps * CF_C * 3; e += blockDim.x) {
+        const int col = e / 3;
+        const int comp = e - col * 3;
+        const float v = col < ncols ? __ldg(src + e) : qnan;
+        const int o = ((col >> 2) * 3 + comp) * CF_C + (col & 3);
+        reinterpret_cast<float2*>(dst)[o] = make_float2(v, v);
+      }
+    }
+    __syncthreads();
+    if (warp_active) {
+#pragma unroll 1
+      for (int s = 0; s < nsteps; ++s) {
+        const ulonglong2* cp = reinterpret_cast<const ulonglong2*>(&s_col[s][0][0]);
+        const ulonglong2 xa = cp[0], xb = cp[1], ya = cp[2], yb = cp[3], za = cp[4], zb = cp[5];
+        const u64 X[CF_C] = {xa.x, xa.y, xb.x, xb.y};
+        const u64 Y[CF_C] = {ya.x, ya.y, yb.x, yb.y};
+        const u64 Z[CF_C] = {za.x, za.y, zb.x, zb.y};
+        float d[CF_C][CF_R];
+#pragma unroll
+        for (int c = 0; c < CF_C; ++c) {
+#pragma unroll
+          for (int p = 0; p < CF_RP; ++p) {
+            const u64 t = dist2x2<MODE>(sub2(X[c], QX[p]), sub2(Y[c], QY[p]), sub2(Z[c], QZ[p]));
+            upk(t, d[c][2 * p], d[c][2 * p + 1]);
+          }
+        }
+        const int colbase = (int)(tc + s * CF_C);
+#pragma unroll
+        for (int r = 0; r < CF_R; ++r) {
+          float nb = min3f(best[r], d[0][r], d[1][r]);
+          nb = min3f(nb, d[2][r], d[3][r]);
+          if (nb < best[r]) bchunk[r] = colbase;
+          best[r] = nb;
+        }
+#pragma unroll
+        for (int c = 0; c < CF_C; ++c) {
+          const float m0 = min3f(d[c][0], d[c][1], d[c][2]);
+          const float m1 = min3f(d[c][3], d[c][4], d[c][5]);
+          const float m2 = min3f(d[c][6], d[c][7], d[c][8]);
+          const float m3 = min3f(d[c][9], d[c][10], d[c][11]);
+          const float m4 = min3f(d[c][12], d[c][13], d[c][14]);
+          const float m5 = min3f(m0, m1, m2);
+          const float m6 = min3f(m3, m4, d[c][15]);
+          const unsigned u = __float_as_uint(fminf(m5, m6));
+          const unsigned w = redux_min_u32(u);
+          const unsigned bal = __ballot_sync(0xffffffffu, u == w);
+          const int win = __ffs(bal) - 1;
+          if (lane == 0)
+            s_key[warp][s * CF_C + c] =
+                ((u64)w << 32) | (unsigned)(warp_row0 + (int64_t)win * CF_R);
+        }
+      }
+    }
+    __syncthreads();
+    for (int col = threadIdx.x; col < ncols; col += blockDim.x) {
+      u64 k = s_key[0][col];
+      for (int w = 1; w < n_active; ++w) k = min(k, s_key[w][col]);
+      red_min_u64(keys2 + b * M + tc + col, k);
+    }
+  }
+  if (warp_active) {
+#pragma unroll
+    for (int r = 0; r < CF_R; ++r) {
+      const int64_t row = lane_row0 + r;
+      if (row < row_end)
+        red_min_u64(keys1 + b * N + row,
+                    ((u64)__float_as_uint(best[r]) << 32) | (unsigned)bchunk[r]);
+    }
+  }
+}
+
+// ------------------------- fp16 / fp64 generic path -------------------------
+// Same decomposition with scalar arithmetic: R = 8 rows per lane.
+constexpr int CG_R = 8;
+constexpr int CG_C = 4;
+constexpr int CG_TILE_STEPS = 64;
+constexpr int CG_TILE = CG_TILE_STEPS * CG_C;
+constexpr int CG_MAXW = 4;
+constexpr int CG_ROWS_PER_WARP = 32 * CG_R;
+
+template <typename T, int MODE>
+struct GenDist;
+template <int MODE>
+struct GenDist<__half, MODE> {
+  using V = float;  // exact float value of the half distance
+  __device__ static float d(__half cx, __half cy, __half cz, __half qx, __half qy, __half qz) {
+    return __half2float(dist1h(hsub_rn(cx, qx), hsub_rn(cy, qy), hsub_rn(cz, qz)));
+  }
+  __device__ static __half nan_() { return __ushort_as_half((unsigned short)0x7fff); }
+};
+template <int MODE>
+struct GenDist<double, MODE> {
+  using V = double;
+  __device__ static double d(double cx, double cy, double cz, double qx, double qy, double qz) {
+    return dist1d<MODE>(__dsub_rn(cx, qx), __dsub_rn(cy, qy), __dsub_rn(cz, qz));
+  }
+  __device__ static double nan_() { return __longlong_as_double(0x7fffffffffffffffll); }
+};
+
+// Key handling for the two value types.
+template <typename V>
+struct KeyOps;
+template <>
+struct KeyOps<float> {
+  using K = u64;
+  __device__ static K make(float v, unsigned chunk) {
+    return ((u64)__float_as_uint(v) << 32) | chunk;
+  }
+  __device__ static K kmin(K a, K b) { return a < b ? a : b; }
+  __device__ static K empty() { return ~0ull; }
+  __device__ static void flush(K* dst, K k) { red_min_u64(dst, k); }
+  // warp argmin of v (>= 0 or NaN): returns min bit pattern key's value and lowest lane
+  __device__ static void warp_argmin(float v, float& wv, int& win) {
+    const unsigned u = __float_as_uint(v);
+    const unsigned w = redux_min_u32(u);
+    win = __ffs(__ballot_sync(0xffffffffu, u == w)) - 1;
+    wv = __uint_as_float(w);
+  }
+};
+template <>
+struct KeyOps<double> {
+  using K = Key128;
+  __device__ static K make(double v, unsigned chunk) {
+    K k;
+    k.hi = (u64)__double_as_longlong(v);
+    k.lo = chunk;
+    return k;
+  }
+  __device__ static K kmin(K a, K b) { return key128_less(b.hi, b.lo, a.hi, a.lo) ? b : a; }
+  __device__ static K empty() {
+    K k;
+    k.hi = ~0ull;
+    k.lo = ~0ull;
+    return k;
+  }
+  __device__ static void flush(K* dst, K k) { key128_min(dst, k.hi, k.lo); }
+  __device__ static void warp_argmin(double v, double& wv, int& win) {
+    const u64 u = (u64)__double_as_longlong(v);
+    const unsigned hi = (unsigned)(u >> 32);
+    const unsigned whi = redux_min_u32(hi);
+    const unsigned lo = (hi == whi) ? (unsigned)u : 0xffffffffu;
+    const unsigned wlo = redux_min_u32(lo);
+    const u64 w = ((u64)whi << 32) | wlo;
+    win = __ffs(__ballot_sync(0xffffffffu, u == w)) - 1;
+    wv = __longlong_as_double((long long)w);
+  }
+};
+
+template <typename T, int MODE>
+__global__ void __launch_bounds__(CG_MAXW * 32)
+    chamfer_keys_generic_kernel(const T* __restrict__ xyz1, const T* __restrict__ xyz2,
+                                int64_t N, int64_t M, int64_t row_begin, int64_t row_end,
+                                int rb_count, int cs_count, int64_t seg,
+                                typename KeyOps<typename GenDist<T, MODE>::V>::K* __restrict__ keys1,
+                                typename KeyOps<typename GenDist<T, MODE>::V>::K* __restrict__ keys2) {
+  using G = GenDist<T, MODE>;
+  using V = typename G::V;
+  using KO = KeyOps<V>;
+  using K = typename KO::K;
+  __shared__ __align__(16) T s_col[CG_TILE_STEPS][3][CG_C];
+  __shared__ __align__(16) K s_key[CG_MAXW][CG_TILE];
+
+  const int W = blockDim.x >> 5;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  int64_t unit = blockIdx.x;
+  const int cs = (int)(unit % cs_count);
+  unit /= cs_count;
+  const int rb = (int)(unit % rb_count);
+  const int64_t b = unit / rb_count;
+  const int64_t c0 = (int64_t)cs * seg;
+  const int64_t c1 = min(M, c0 + seg);
+  const int64_t blk_row0 = row_begin + (int64_t)rb * W * CG_ROWS_PER_WARP;
+  const int64_t warp_row0 = blk_row0 + (int64_t)warp * CG_ROWS_PER_WARP;
+  const int64_t lane_row0 = warp_row0 + (int64_t)lane * CG_R;
+  const bool warp_active = warp_row0 < row_end;
+  const int n_active = (int)min64(W, (row_end - blk_row0 + CG_ROWS_PER_WARP - 1) / CG_ROWS_PER_WARP);
+
+  T qx[CG_R], qy[CG_R], qz[CG_R];
+#pragma unroll
+  for (int r = 0; r < CG_R; ++r) {
+    const bool ok = lane_row0 + r < row_end;
+    const T* a = xyz1 + (b * N + lane_row0 + r) * 3;
+    qx[r] = ok ? a[0] : G::nan_();
+    qy[r] = ok ? a[1] : G::nan_();
+    qz[r] = ok ? a[2] : G::nan_();
+  }
+  V best[CG_R];
+  int bchunk[CG_R];
+#pragma unroll
+  for (int r = 0; r < CG_R; ++r) {
+    best[r] = (V)INFINITY;
+    bchunk[r] = 0;
+  }
+
+  for (int64_t tc = c0; tc < c1; tc += CG_TILE) {
+    const int ncols = (int)min64(CG_TILE, c1 - tc);
+    const int nsteps = (ncols + CG_C - 1) / CG_C;
+    __syncthreads();
+    {
+      const T* src = xyz2 + (b * M + tc) * 3;
+      T* dst = &s_col[0][0][0];
+      for (int e = threadIdx.x; e < nsteps * CG_C * 3; e += blockDim.x) {
+        const int col = e / 3;
+        const int comp = e - col * 3;
+        dst[((col >> 2) * 3 + comp) * CG_C + (col & 3)] = col < ncols ? src[e] : G::nan_();
+      }
+    }
+    __syncthreads();
+    if (warp_active) {
+#pragma unroll 1
+      for (int s = 0; s < nsteps; ++s) {
+        V d[CG_C][CG_R];
+#pragma unroll
+        for (int c = 0; c < CG_C; ++c) {
+          const T cx = s_col[s][0][c], cy = s_col[s][1][c], cz = s_col[s][2][c];
+#pragma unroll
+          for (int r = 0; r < CG_R; ++r) d[c][r] = G::d(cx, cy, cz, qx[r], qy[r], qz[r]);
+        }
+        const int colbase = (int)(tc + s * CG_C);
+#pragma unroll
+        for (int r = 0; r < CG_R; ++r) {
+          const V nb = fmin(fmin(best[r], fmin(d[0][r], d[1][r])), fmin(d[2][r], d[3][r]));
+          if (nb < best[r]) bchunk[r] = colbase;
+          best[r] = nb;
+        }
+#pragma unroll
+        for (int c = 0; c < CG_C; ++c) {
+          V m = d[c][0];
+#pragma unroll
+          for (int r = 1; r < CG_R; ++r) m = fmin(m, d[c][r]);
+          V wv;
+          int win;
+          KO::warp_argmin(m, wv, win);
+          if (lane == 0)
+            s_key[warp][s * CG_C + c] = KO::make(wv, (unsigned)(warp_row0 + (int64_t)win * CG_R));
+        }
+      }
+    }
+    __syncthreads();
+    for (int col = threadIdx.x; col < ncols; col += blockDim.x) {
+      K k = s_key[0][col];
+      for (int w = 1; w < n_active; ++w) k = KO::kmin(k, s_key[w][col]);
+      KO::flush(keys2 + b * M + tc + col, k);
+    }
+  }
+  if (warp_active) {
+#pragma unroll
+    for (int r = 0; r < CG_R; ++r) {
+      const int64_t row = lane_row0 + r;
+      if (row < row_end) KO::flush(keys1 + b * N + row, KO::make(best[r], (unsigned)bchunk[r]));
+    }
+  }
+}
+
+// ------------------------------- finalize -------------------------------
+template <typename T>
+struct FinTraits;
+template <>
+struct FinTraits<float> {
+  using K = u64;
+  template <int MODE>
+  __device__ static bool same(const float* a, const float* c, K key) {
+    const float d = dist1f<MODE>(__fsub_rn(c[0], a[0]), __fsub_rn(c[1], a[1]), __fsub_rn(c[2], a[2]));
+    return __float_as_uint(d) == (unsigned)(key >> 32);
+  }
+  __device__ static bool empty(K k) { return k == ~0ull; }
+  __device__ static unsigned chunk(K k) { return (unsigned)k; }
+  __device__ static float value(K k) { return __uint_as_float((unsigned)(k >> 32)); }
+};
+template <>
+struct FinTraits<__half> {
+  using K = u64;
+  template <int MODE>
+  __device__ static bool same(const __half* a, const __half* c, K key) {
+    const float d = __half2float(dist1h(hsub_rn(c[0], a[0]), hsub_rn(c[1], a[1]), hsub_rn(c[2], a[2])));
+    return __float_as_uint(d) == (unsigned)(key >> 32);
+  }
+  __device__ static bool empty(K k) { return k == ~0ull; }
+  __device__ static unsigned chunk(K k) { return (unsigned)k; }
+  __device__ static __half value(K k) { return __float2half_rn(__uint_as_float((unsigned)(k >> 32))); }
+};
+template <>
+struct FinTraits<double> {
+  using K = Key128;
+  template <int MODE>
+  __device__ static bool same(const double* a, const double* c, K key) {
+    const double d = dist1d<MODE>(__dsub_rn(c[0], a[0]), __dsub_rn(c[1], a[1]), __dsub_rn(c[2], a[2]));
+    return (u64)__double_as_longlong(d) == key.hi;
+  }
+  __device__ static bool empty(K k) { return k.hi == ~0ull && k.lo == ~0ull; }
+  __device__ static unsigned chunk(K k) { return (unsigned)k.lo; }
+  __device__ static double value(K k) { return __longlong_as_double((long long)k.hi); }
+};
+
+// One thread per output point.  Rows: key chunk = first of `row_chunk` columns
+// (4).  Columns: key chunk = first of `col_chunk` rows (R of the keys kernel).
+template <typename T, int MODE>
+__global__ void chamfer_finalize_kernel(const T* __restrict__ xyz1, const T* __restrict__ xyz2,
+                                        int64_t B, int64_t N, int64_t M, int64_t row_begin,
+                                        int64_t row_end, int row_chunk, int col_chunk,
+                                        const typename FinTraits<T>::K* __restrict__ keys1,
+                                        const typename FinTraits<T>::K* __restrict__ keys2,
+                                        T* __restrict__ dist1, int32_t* __restrict__ idx1,
+                                        T* __restrict__ dist2, int32_t* __restrict__ idx2) {
+  using F = FinTraits<T>;
+  const int64_t nrows = row_end - row_begin;
+  const int64_t n1 = B * nrows;
+  const int64_t total = n1 + (dist2 ? B * M : 0);
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    if (t < n1) {
+      const int64_t b = t / nrows, i = row_begin + t % nrows;
+      const int64_t o = b * N + i;
+      const typename F::K key = keys1[o];
+      T dv = T(0.0f);
+      int32_t ix = 0;
+      if (M > 0 && !F::empty(key)) {
+        const unsigned base = F::chunk(key);
+        const T* a = xyz1 + o * 3;
+        ix = (int32_t)base;
+        const int64_t end = min64(M, (int64_t)base + row_chunk);
+        for (int64_t j = base; j < end; ++j)
+          if (F::template same<MODE>(a, xyz2 + (b * M + j) * 3, key)) { ix = (int32_t)j; break; }
+        dv = F::value(key);
+      }
+      dist1[o] = dv;
+      idx1[o] = ix;
+    } else {
+      const int64_t u = t - n1;
+      const int64_t b = u / M, j = u % M;
+      const int64_t o = b * M + j;
+      const typename F::K key = keys2[o];
+      T dv = T(0.0f);
+      int32_t ix = 0;
+      if (N > 0 && !F::empty(key)) {
+        const unsigned base = F::chunk(key);
+        const T* c = xyz2 + o * 3;
+        ix = (int32_t)base;
+        const int64_t end = min64(N, (int64_t)base + col_chunk);
+        for (int64_t i = base; i < end; ++i)
+          if (F::template same<MODE>(xyz1 + (b * N + i) * 3, c, key)) { ix = (int32_t)i; break; }
+        dv = F::value(key);
+      }
+      dist2[o] = dv;
+      idx2[o] = ix;
+    }
+  }
+}
+
+// ------------------------------- host side -------------------------------
+namespace {
+
+struct Plan {
+  int warps, rb_count, cs_count;
+  int64_t seg;
+  int64_t ctas;
+};
+
+// Column-segment count: enough CTAs to fill every SM several times over while
+// keeping segments long enough to amortise the per-unit row load / flush.
+Plan make_plan(int64_t B, int64_t nrows, int64_t M, int rows_per_warp, int max_warps, int slots) {
+  Plan p;
+  const int64_t warps_needed = (nrows + rows_per_warp - 1) / rows_per_warp;
+  p.warps = (int)std::max<int64_t>(1, std::min<int64_t>(max_warps, warps_needed));
+  p.rb_count = (int)((warps_needed + p.warps - 1) / p.warps);
+  const int64_t base = B * p.rb_count;
+  const int64_t max_cs = std::max<int64_t>(1, (M + 63) / 64);
+  // cost model: waves * (columns per unit + fixed overhead in column units)
+  double best = 1e300;
+  int64_t best_cs = 1;
+  const int64_t lim = std::min<int64_t>(max_cs, 4096);
+  for (int64_t cs = 1; cs <= lim; ++cs) {
+    const int64_t seg = ((M + cs - 1) / cs + 3) / 4 * 4;
+    const int64_t real_cs = (M + seg - 1) / seg;
+    if (real_cs != cs) continue;
+    const int64_t units = base * cs;
+    const double waves = (double)((units + slots - 1) / slots);
+    const double cost = waves * (double)(seg + 96);
+    if (cost < best * 0.999) {
+      best = cost;
+      best_cs = cs;
+    }
+  }
+  p.seg = std::max<int64_t>(4, ((M + best_cs - 1) / best_cs + 3) / 4 * 4);
+  p.cs_count = (int)((M + p.seg - 1) / p.seg);
+  p.ctas = base * p.cs_count;
+  return p;
+}
+
+template <typename KernelT>
+int slots_for(KernelT kernel, int threads) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int sms = 0, per_sm = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, 0);
+  return std::max(1, sms * std::max(1, per_sm));
+}
+
+template <int MODE>
+int launch_keys_f32(const float* x1, const float* x2, int64_t B, int64_t N, int64_t M,
+                    int64_t rb0, int64_t rb1, void* k1, void* k2, cudaStream_t st) {
+  auto kern = chamfer_keys_f32_kernel<MODE>;
+  static thread_local int slots_cache[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int& slots = slots_cache[dev & 63];
+  if (!slots) slots = slots_for(kern, CF_MAXW * 32);
+  const Plan p = make_plan(B, rb1 - rb0, M, CF_ROWS_PER_WARP, CF_MAXW, slots);
+  if (p.ctas <= 0) return TPO_OK;
+  kern<<<(unsigned)p.ctas, p.warps * 32, 0, st>>>(x1, x2, N, M, rb0, rb1, p.rb_count, p.cs_count,
+                                                   p.seg, (u64*)k1, (u64*)k2);
+  return check_launch();
+}
+
+template <typename T, int MODE>
+int launch_keys_generic(const T* x1, const T* x2, int64_t B, int64_t N, int64_t M, int64_t rb0,
+                        int64_t rb1, void* k1, void* k2, cudaStream_t st) {
+  using K = typename KeyOps<typename GenDist<T, MODE>::V>::K;
+  auto kern = chamfer_keys_generic_kernel<T, MODE>;
+  static thread_local int slots_cache[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int& slots = slots_cache[dev & 63];
+  if (!slots) slots = slots_for(kern, CG_MAXW * 32);
+  const Plan p = make_plan(B, rb1 - rb0, M, CG_ROWS_PER_WARP, CG_MAXW, slots);
+  if (p.ctas <= 0) return TPO_OK;
+  kern<<<(unsigned)p.ctas, p.warps * 32, 0, st>>>(x1, x2, N, M, rb0, rb1, p.rb_count, p.cs_count,
+                                                   p.seg, (K*)k1, (K*)k2);
+  return check_launch();
+}
+
+template <typename T, int MODE>
+int launch_finalize(const T* x1, const T* x2, int64_t B, int64_t N, int64_t M, int64_t rb0,
+                    int64_t rb1, int col_chunk, const void* k1, const void* k2, T* d1, int32_t* i1,
+                    T* d2, int32_t* i2, cudaStream_t st) {
+  const int64_t total = B * (rb1 - rb0) + (d2 ? B * M : 0);
+  if (total <= 0) return TPO_OK;
+  const int threads = 256;
+  const int64_t blocks = std::min<int64_t>((total + threads - 1) / threads, 148 * 32);
+  chamfer_finalize_kernel<T, MODE><<<(unsigned)blocks, threads, 0, st>>>(
+      x1, x2, B, N, M, rb0, rb1, CF_C, col_chunk, (const typename FinTraits<T>::K*)k1,
+      (const typename FinTraits<T>::K*)k2, d1, i1, d2, i2);
+  return check_launch();
+}
+
+}  // namespace
+
+int chamfer_fwd_keys(int dtype, int flags, const void* x1, const void* x2, int64_t B, int64_t N,
+                     int64_t M, int64_t rb0, int64_t rb1, void* k1, void* k2, cudaStream_t st) {
+  const bool exact = (flags & TPO_ROUND_EXACT) != 0;
+  if (B == 0 || rb1 <= rb0 || M == 0) return TPO_OK;
+  switch (dtype) {
+    case TPO_F32:
+      return exact ? launch_keys_f32<TPO_ROUND_EXACT>((const float*)x1, (const float*)x2, B, N, M, rb0, rb1, k1, k2, st)
+                   : launch_keys_f32<TPO_ROUND_FMA>((const float*)x1, (const float*)x2, B, N, M, rb0, rb1, k1, k2, st);
+    case TPO_F16:
+      return launch_keys_generic<__half, TPO_ROUND_EXACT>((const __half*)x1, (const __half*)x2, B, N, M, rb0, rb1, k1, k2, st);
+    case TPO_F64:
+      return exact ? launch_keys_generic<double, TPO_ROUND_EXACT>((const double*)x1, (const double*)x2, B, N, M, rb0, rb1, k1, k2, st)
+                   : launch_keys_generic<double, TPO_ROUND_FMA>((const double*)x1, (const double*)x2, B, N, M, rb0, rb1, k1, k2, st);
+  }
+  return TPO_ERR_INVALID_ARGUMENT;
+}
+
+int chamfer_finalize(int dtype, int flags, const void* x1, const void* x2, int64_t B, int64_t N,
+                     int64_t M, int64_t rb0, int64_t rb1, const void* k1, const void* k2, void* d1,
+                     int32_t* i1, void* d2, int32_t* i2, cudaStream_t st) {
+  const bool exact = (flags & TPO_ROUND_EXACT) != 0;
+  switch (dtype) {
+    case TPO_F32:
+      return exact ? launch_finalize<float, TPO_ROUND_EXACT>((const float*)x1, (const float*)x2, B, N, M, rb0, rb1, CF_R, k1, k2, (float*)d1, i1, (float*)d2, i2, st)
+                   : launch_finalize<float, TPO_ROUND_FMA>((const float*)x1, (const float*)x2, B, N, M, rb0, rb1, CF_R, k1, k2, (float*)d1, i1, (float*)d2, i2, st);
+    case TPO_F16:
+      return launch_finalize<__half, TPO_ROUND_EXACT>((const __half*)x1, (const __half*)x2, B, N, M, rb0, rb1, CG_R, k1, k2, (__half*)d1, i1, (__half*)d2, i2, st);
+    case TPO_F64:
+      return exact ? launch_finalize<double, TPO_ROUND_EXACT>((const double*)x1, (const double*)x2, B, N, M, rb0, rb1, CG_R, k1, k2, (double*)d1, i1, (double*)d2, i2, st)
+                   : launch_finalize<double, TPO_ROUND_FMA>((const double*)x1, (const double*)x2, B, N, M, rb0, rb1, CG_R, k1, k2, (double*)d1, i1, (double*)d2, i2, st);
+  }
+  return TPO_ERR_INVALID_ARGUMENT;
+}
+
+}  // namespace tpo

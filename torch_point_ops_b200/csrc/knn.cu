@@ -1,0 +1,411 @@
+// K nearest neighbours (forward + backward) and knn_gather for sm_100a.
+//
+// Forward replaces knn_cuda_forward + KNearestNeighborKernelV0..V3
+// (torch_point_ops/knn/csrc/cuda/knn.cu:16-227,295-398) and the host-side sort
+// of knn_points (knn/__init__.py:110-131).  A warp serves KQ queries of one
+// batch; its 32 lanes evaluate 32 consecutive target points per step (staged in
+// shared memory, shared by the CTA's warps).  Each query's running top-K list is
+// distributed across the warp (lane k holds the k-th best), so:
+//   * filtering is one compare + ballot per query per step against the K-th
+//     distance (kept uniform in a register);
+//   * a surviving candidate is inserted with one shuffle-up shift of the list.
+// Candidates are inserted in increasing index order and a candidate equal to an
+// existing distance lands after it, and one equal to the K-th is rejected, so
+// the list is exactly "K smallest by (dist, idx), ascending": the reference CPU
+// priority_queue result (knn.cpp:61-95).  Output is sorted in the kernel; the
+// torch.sort + mask pass of the reference disappears.
+//
+// Backward replaces KNearestNeighborBackwardKernel (knn.cu:401-466): one thread
+// per query row sums its K terms in k order (deterministic, no atomics for
+// grad_p1) and scatters the negated terms into grad_p2 with atomics.
+#include "tpo_internal.h"
+
+namespace tpo {
+
+constexpr int KQ = 8;        // queries per warp
+constexpr int KW = 4;        // warps per CTA
+constexpr int KSTEP = 32;    // targets per step (one per lane)
+constexpr int KTILE = 256;   // targets per shared-memory tile
+constexpr int KDMAX = 8;
+
+template <typename T>
+struct KnnArith;
+template <>
+struct KnnArith<float> {
+  using V = float;
+  template <int MODE>
+  __device__ static float sq_first(float a, float b) {
+    const float d = __fsub_rn(a, b);
+    return __fmul_rn(d, d);
+  }
+  template <int MODE>
+  __device__ static float sq_acc(float t, float a, float b) {
+    const float d = __fsub_rn(a, b);
+    return MODE == TPO_ROUND_FMA ? __fmaf_rn(d, d, t) : __fadd_rn(t, __fmul_rn(d, d));
+  }
+  __device__ static float abs_first(float a, float b) { return fabsf(__fsub_rn(a, b)); }
+  __device__ static float abs_acc(float t, float a, float b) { return __fadd_rn(t, fabsf(__fsub_rn(a, b))); }
+  __device__ static V val(float x) { return x; }
+  __device__ static float from(V v) { return v; }
+  __device__ static float nan_() { return __int_as_float(0x7fffffff); }
+};
+template <>
+struct KnnArith<double> {
+  using V = double;
+  template <int MODE>
+  __device__ static double sq_first(double a, double b) {
+    const double d = __dsub_rn(a, b);
+    return __dmul_rn(d, d);
+  }
+  template <int MODE>
+  __device__ static double sq_acc(double t, double a, double b) {
+    const double d = __dsub_rn(a, b);
+    return MODE == TPO_ROUND_FMA ? __fma_rn(d, d, t) : __dadd_rn(t, __dmul_rn(d, d));
+  }
+  __device__ static double abs_first(double a, double b) { return fabs(__dsub_rn(a, b)); }
+  __device__ static double abs_acc(double t, double a, double b) { return __dadd_rn(t, fabs(__dsub_rn(a, b))); }
+  __device__ static V val(double x) { return x; }
+  __device__ static double from(V v) { return v; }
+  __device__ static double nan_() { return __longlong_as_double(0x7fffffffffffffffll); }
+};
+template <>
+struct KnnArith<__half> {
+  using V = float;  // exact float image of the half result
+  template <int MODE>
+  __device__ static __half sq_first(__half a, __half b) {
+    const __half d = hsub_rn(a, b);
+    return hmul_rn(d, d);
+  }
+  template <int MODE>
+  __device__ static __half sq_acc(__half t, __half a, __half b) {
+    const __half d = hsub_rn(a, b);
+    return hadd_rn(t, hmul_rn(d, d));
+  }
+  __device__ static __half abs_first(__half a, __half b) { return __habs(hsub_rn(a, b)); }
+  __device__ static __half abs_acc(__half t, __half a, __half b) { return hadd_rn(t, __habs(hsub_rn(a, b))); }
+  __device__ static V val(__half x) { return __half2float(x); }
+  __device__ static __half from(V v) { return __float2half_rn(v); }
+  __device__ static __half nan_() { return __ushort_as_half((unsigned short)0x7fff); }
+};
+
+template <typename T, int DT, int NORM, int MODE>
+__device__ __forceinline__ typename KnnArith<T>::V knn_dist(const T* q, const T* c, int D) {
+  using A = KnnArith<T>;
+  const int Dn = DT > 0 ? DT : D;
+  T t = NORM == 2 ? A::template sq_first<MODE>(q[0], c[0]) : A::abs_first(q[0], c[0]);
+#pragma unroll
+  for (int d = 1; d < (DT > 0 ? DT : KDMAX); ++d) {
+    if (d < Dn) t = NORM == 2 ? A::template sq_acc<MODE>(t, q[d], c[d]) : A::abs_acc(t, q[d], c[d]);
+  }
+  return A::val(t);
+}
+
+template <typename T, int DT, int NORM, int MODE>
+__global__ void __launch_bounds__(KW * 32)
+    knn_fwd_kernel(const T* __restrict__ p1, const T* __restrict__ p2,
+                   const int64_t* __restrict__ len1, const int64_t* __restrict__ len2, int64_t N,
+                   int64_t P1, int64_t P2, int D, int K, int qblocks, T* __restrict__ dists,
+                   int64_t* __restrict__ idxs) {
+  using A = KnnArith<T>;
+  using V = typename A::V;
+  constexpr int DC = DT > 0 ? DT : KDMAX;
+  __shared__ T s_c[KTILE][DC];
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t n = blockIdx.x / qblocks;
+  const int64_t q0 = (int64_t)(blockIdx.x % qblocks) * (KW * KQ) + warp * KQ;
+  const int64_t L1 = len1 ? min64(max64(len1[n], 0), P1) : P1;
+  const int64_t L2 = len2 ? min64(max64(len2[n], 0), P2) : P2;
+  const int Dn = DT > 0 ? DT : D;
+
+  T q[KQ][DC];
+  bool qv[KQ];
+#pragma unroll
+  for (int i = 0; i < KQ; ++i) {
+    qv[i] = q0 + i < L1;
+#pragma unroll
+    for (int d = 0; d < DC; ++d)
+      q[i][d] = (qv[i] && d < Dn) ? p1[(n * P1 + q0 + i) * Dn + d] : T(0.0f);
+  }
+  V Ld[KQ], thr[KQ];
+  int Li[KQ];
+#pragma unroll
+  for (int i = 0; i < KQ; ++i) {
+    Ld[i] = (V)INFINITY;
+    Li[i] = -1;
+    thr[i] = (V)INFINITY;
+  }
+  const bool any_q = q0 < L1;
+  const int64_t blk_q0 = (int64_t)(blockIdx.x % qblocks) * (KW * KQ);
+  const bool blk_active = blk_q0 < L1;
+
+  if (blk_active) {
+    for (int64_t t0 = 0; t0 < L2; t0 += KTILE) {
+      const int nt = (int)min64(KTILE, L2 - t0);
+      __syncthreads();
+      {
+        const T* src = p2 + (n * P2 + t0) * Dn;
+        for (int e = threadIdx.x; e < nt * Dn; e += blockDim.x) {
+          const int c = e / Dn, d = e - c * Dn;
+          s_c[c][d] = src[e];
+        }
+      }
+      __syncthreads();
+      if (any_q) {
+        const int nsteps = (nt + KSTEP - 1) / KSTEP;
+#pragma unroll 1
+        for (int s = 0; s < nsteps; ++s) {
+          const int c = s * KSTEP + lane;
+          const bool cv = c < nt;
+          T cc[DC];
+#pragma unroll
+          for (int d = 0; d < DC; ++d) cc[d] = (cv && d < Dn) ? s_c[c][d] : T(0.0f);
+          const int cidx = (int)(t0 + c);
+#pragma unroll
+          for (int i = 0; i < KQ; ++i) {
+            if (!qv[i]) continue;  // warp-uniform
+            const V dv = knn_dist<T, DT, NORM, MODE>(q[i], cc, Dn);
+            unsigned bal = __ballot_sync(0xffffffffu, cv && dv < thr[i]);
+            while (bal) {
+              const int src = __ffs(bal) - 1;
+              bal &= bal - 1;
+              const V cd = __shfl_sync(0xffffffffu, dv, src);
+              if (cd < thr[i]) {
+                const int ci = cidx - lane + src;
+                const V upd = __shfl_up_sync(0xffffffffu, Ld[i], 1);
+                const int upi = __shfl_up_sync(0xffffffffu, Li[i], 1);
+                if (cd < Ld[i]) {
+                  const bool take_prev = lane > 0 && cd < upd;
+                  Ld[i] = take_prev ? upd : cd;
+                  Li[i] = take_prev ? upi : ci;
+                }
+                thr[i] = __shfl_sync(0xffffffffu, Ld[i], K - 1);
+              }
+            }
+          }
+        }
+      }
+    }
+  }
+  // write-out: every row of this warp's range, valid or padding
+  if (lane < K) {
+#pragma unroll
+    for (int i = 0; i < KQ; ++i) {
+      const int64_t row = q0 + i;
+      if (row >= P1) break;
+      const int64_t o = (n * P1 + row) * K + lane;
+      const bool ok = qv[i] && Li[i] >= 0;
+      dists[o] = ok ? A::from(Ld[i]) : T(0.0f);
+      idxs[o] = ok ? (int64_t)Li[i] : -1;
+    }
+  }
+}
+
+template <typename T, int DT, int NORM, int MODE>
+static int launch_knn_fwd(const T* p1, const T* p2, const int64_t* l1, const int64_t* l2, int64_t N,
+                          int64_t P1, int64_t P2, int D, int K, T* dists, int64_t* idxs,
+                          cudaStream_t st) {
+  const int qblocks = (int)((P1 + KW * KQ - 1) / (KW * KQ));
+  const int64_t ctas = N * qblocks;
+  if (ctas <= 0) return TPO_OK;
+  knn_fwd_kernel<T, DT, NORM, MODE><<<(unsigned)ctas, KW * 32, 0, st>>>(p1, p2, l1, l2, N, P1, P2, D,
+                                                                       K, qblocks, dists, idxs);
+  return check_launch();
+}
+
+template <typename T, int MODE>
+static int dispatch_knn_fwd(const void* p1, const void* p2, const int64_t* l1, const int64_t* l2,
+                            int64_t N, int64_t P1, int64_t P2, int64_t D, int64_t norm, int64_t K,
+                            void* dists, int64_t* idxs, cudaStream_t st) {
+  const T* a = (const T*)p1;
+  const T* b = (const T*)p2;
+  T* o = (T*)dists;
+  if (D == 3)
+    return norm == 2 ? launch_knn_fwd<T, 3, 2, MODE>(a, b, l1, l2, N, P1, P2, 3, (int)K, o, idxs, st)
+                     : launch_knn_fwd<T, 3, 1, MODE>(a, b, l1, l2, N, P1, P2, 3, (int)K, o, idxs, st);
+  return norm == 2 ? launch_knn_fwd<T, 0, 2, MODE>(a, b, l1, l2, N, P1, P2, (int)D, (int)K, o, idxs, st)
+                   : launch_knn_fwd<T, 0, 1, MODE>(a, b, l1, l2, N, P1, P2, (int)D, (int)K, o, idxs, st);
+}
+
+int knn_forward(int dtype, int flags, const void* p1, const void* p2, const int64_t* l1,
+                const int64_t* l2, int64_t N, int64_t P1, int64_t P2, int64_t D, int64_t norm,
+                int64_t K, void* dists, int64_t* idxs, cudaStream_t st) {
+  if (D > KDMAX || K > 32) return TPO_ERR_UNSUPPORTED;
+  const bool exact = (flags & TPO_ROUND_EXACT) != 0;
+  switch (dtype) {
+    case TPO_F32:
+      return exact ? dispatch_knn_fwd<float, TPO_ROUND_EXACT>(p1, p2, l1, l2, N, P1, P2, D, norm, K, dists, idxs, st)
+                   : dispatch_knn_fwd<float, TPO_ROUND_FMA>(p1, p2, l1, l2, N, P1, P2, D, norm, K, dists, idxs, st);
+    case TPO_F16:
+      return dispatch_knn_fwd<__half, TPO_ROUND_EXACT>(p1, p2, l1, l2, N, P1, P2, D, norm, K, dists, idxs, st);
+    case TPO_F64:
+      return exact ? dispatch_knn_fwd<double, TPO_ROUND_EXACT>(p1, p2, l1, l2, N, P1, P2, D, norm, K, dists, idxs, st)
+                   : dispatch_knn_fwd<double, TPO_ROUND_FMA>(p1, p2, l1, l2, N, P1, P2, D, norm, K, dists, idxs, st);
+  }
+  return TPO_ERR_INVALID_ARGUMENT;
+}
+
+// ------------------------------- backward -------------------------------
+template <typename T>
+struct KbOps;
+template <>
+struct KbOps<float> {
+  __device__ static float l2(float g, float a, float b) { return __fmul_rn(__fmul_rn(g, 2.0f), __fsub_rn(a, b)); }
+  __device__ static float l1(float g, float a, float b) { return a > b ? g : (a == b ? 0.0f : -g); }
+  __device__ static float add(float a, float b) { return __fadd_rn(a, b); }
+  __device__ static void atomic_sub(float* p, float v) { atomicAdd(p, -v); }
+  __device__ static float zero() { return 0.0f; }
+};
+template <>
+struct KbOps<double> {
+  __device__ static double l2(double g, double a, double b) { return __dmul_rn(__dmul_rn(g, 2.0), __dsub_rn(a, b)); }
+  __device__ static double l1(double g, double a, double b) { return a > b ? g : (a == b ? 0.0 : -g); }
+  __device__ static double add(double a, double b) { return __dadd_rn(a, b); }
+  __device__ static void atomic_sub(double* p, double v) { atomicAdd(p, -v); }
+  __device__ static double zero() { return 0.0; }
+};
+template <>
+struct KbOps<__half> {
+  __device__ static __half l2(__half g, __half a, __half b) {
+    return hmul_rn(hmul_rn(g, __float2half_rn(2.0f)), hsub_rn(a, b));
+  }
+  __device__ static __half l1(__half g, __half a, __half b) {
+    const float fa = __half2float(a), fb = __half2float(b);
+    return fa > fb ? g : (fa == fb ? __float2half_rn(0.0f) : __hneg(g));
+  }
+  __device__ static __half add(__half a, __half b) { return hadd_rn(a, b); }
+  __device__ static void atomic_sub(__half* p, __half v) { atomicAdd(p, __hneg(v)); }
+  __device__ static __half zero() { return __float2half_rn(0.0f); }
+};
+
+template <typename T>
+__global__ void knn_bwd_kernel(const T* __restrict__ p1, const T* __restrict__ p2,
+                               const int64_t* __restrict__ len1, const int64_t* __restrict__ len2,
+                               const int64_t* __restrict__ idxs, int64_t N, int64_t P1, int64_t P2,
+                               int D, int K, int norm, const T* __restrict__ gd,
+                               T* __restrict__ g1, T* __restrict__ g2) {
+  using O = KbOps<T>;
+  const int64_t total = N * P1;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t n = t / P1, i = t % P1;
+    const int64_t L1 = len1 ? len1[n] : P1;
+    const int64_t L2 = len2 ? len2[n] : P2;
+    const int kk = (int)min64(K, max64(L2, 0));
+    T acc[KDMAX];
+#pragma unroll
+    for (int d = 0; d < KDMAX; ++d) acc[d] = O::zero();
+    if (i < L1) {
+      for (int k = 0; k < kk; ++k) {
+        const int64_t j = idxs[t * K + k];
+        if (j < 0 || j >= P2) continue;
+        const T g = gd[t * K + k];
+#pragma unroll
+        for (int d = 0; d < KDMAX; ++d) {
+          if (d < D) {
+            const T a = p1[t * D + d], b = p2[(n * P2 + j) * D + d];
+            const T v = norm == 1 ? O::l1(g, a, b) : O::l2(g, a, b);
+            acc[d] = O::add(acc[d], v);
+            O::atomic_sub(g2 + (n * P2 + j) * D + d, v);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int d = 0; d < KDMAX; ++d)
+      if (d < D) g1[t * D + d] = acc[d];
+  }
+}
+
+int knn_backward(int dtype, const void* p1, const void* p2, const int64_t* l1, const int64_t* l2,
+                 const int64_t* idxs, int64_t N, int64_t P1, int64_t P2, int64_t D, int64_t K,
+                 int64_t norm, const void* gd, void* g1, void* g2, cudaStream_t st) {
+  if (D > KDMAX) return TPO_ERR_UNSUPPORTED;
+  const int64_t total = N * P1;
+  if (total <= 0) return TPO_OK;
+  const int threads = 256;
+  const unsigned blocks = (unsigned)std::min<int64_t>((total + threads - 1) / threads, 148 * 16);
+#define TPO_KB(T)                                                                              \
+  knn_bwd_kernel<T><<<blocks, threads, 0, st>>>((const T*)p1, (const T*)p2, l1, l2, idxs, N, P1, \
+                                                P2, (int)D, (int)K, (int)norm, (const T*)gd,    \
+                                                (T*)g1, (T*)g2)
+  switch (dtype) {
+    case TPO_F32: TPO_KB(float); break;
+    case TPO_F16: TPO_KB(__half); break;
+    case TPO_F64: TPO_KB(double); break;
+    default: return TPO_ERR_INVALID_ARGUMENT;
+  }
+#undef TPO_KB
+  return check_launch();
+}
+
+// ------------------------------- knn_gather -------------------------------
+// out[n,l,k,u] = x[n, idx[n,l,k], u]; zero when k >= lengths[n] or idx invalid.
+template <typename T>
+__global__ void knn_gather_fwd_kernel(const T* __restrict__ x, const int64_t* __restrict__ idx,
+                                      const int64_t* __restrict__ lengths, int64_t N, int64_t M,
+                                      int64_t U, int64_t L, int64_t K, T* __restrict__ out) {
+  const int64_t total = N * L * K * U;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t u = t % U;
+    const int64_t e = t / U;  // (n, l, k)
+    const int64_t k = e % K;
+    const int64_t n = e / (L * K);
+    const int64_t len = lengths ? lengths[n] : M;
+    const int64_t j = idx[e];
+    out[t] = (k < len && j >= 0 && j < M) ? x[(n * M + j) * U + u] : T(0.0f);
+  }
+}
+
+template <typename T>
+__global__ void knn_gather_bwd_kernel(const T* __restrict__ gout, const int64_t* __restrict__ idx,
+                                      const int64_t* __restrict__ lengths, int64_t N, int64_t M,
+                                      int64_t U, int64_t L, int64_t K, T* __restrict__ gx) {
+  const int64_t total = N * L * K * U;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t u = t % U;
+    const int64_t e = t / U;
+    const int64_t k = e % K;
+    const int64_t n = e / (L * K);
+    const int64_t len = lengths ? lengths[n] : M;
+    const int64_t j = idx[e];
+    if (k < len && j >= 0 && j < M) atomicAdd(gx + (n * M + j) * U + u, gout[t]);
+  }
+}
+
+int knn_gather_forward(int dtype, const void* x, const int64_t* idx, const int64_t* lengths,
+                       int64_t N, int64_t M, int64_t U, int64_t L, int64_t K, void* out,
+                       cudaStream_t st) {
+  const int64_t total = N * L * K * U;
+  if (total <= 0) return TPO_OK;
+  const int threads = 256;
+  const unsigned blocks = (unsigned)std::min<int64_t>((total + threads - 1) / threads, 148 * 16);
+  switch (dtype) {
+    case TPO_F32: knn_gather_fwd_kernel<float><<<blocks, threads, 0, st>>>((const float*)x, idx, lengths, N, M, U, L, K, (float*)out); break;
+    case TPO_F16: knn_gather_fwd_kernel<__half><<<blocks, threads, 0, st>>>((const __half*)x, idx, lengths, N, M, U, L, K, (__half*)out); break;
+    case TPO_F64: knn_gather_fwd_kernel<double><<<blocks, threads, 0, st>>>((const double*)x, idx, lengths, N, M, U, L, K, (double*)out); break;
+    default: return TPO_ERR_INVALID_ARGUMENT;
+  }
+  return check_launch();
+}
+
+int knn_gather_backward(int dtype, const void* gout, const int64_t* idx, const int64_t* lengths,
+                        int64_t N, int64_t M, int64_t U, int64_t L, int64_t K, void* gx,
+                        cudaStream_t st) {
+  const int64_t total = N * L * K * U;
+  if (total <= 0) return TPO_OK;
+  const int threads = 256;
+  const unsigned blocks = (unsigned)std::min<int64_t>((total + threads - 1) / threads, 148 * 16);
+  switch (dtype) {
+    case TPO_F32: knn_gather_bwd_kernel<float><<<blocks, threads, 0, st>>>((const float*)gout, idx, lengths, N, M, U, L, K, (float*)gx); break;
+    case TPO_F16: knn_gather_bwd_kernel<__half><<<blocks, threads, 0, st>>>((const __half*)gout, idx, lengths, N, M, U, L, K, (__half*)gx); break;
+    case TPO_F64: knn_gather_bwd_kernel<double><<<blocks, threads, 0, st>>>((const double*)gout, idx, lengths, N, M, U, L, K, (double*)gx); break;
+    default: return TPO_ERR_INVALID_ARGUMENT;
+  }
+  return check_launch();
+}
+
+}  // namespace tpo

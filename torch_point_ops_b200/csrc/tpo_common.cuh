@@ -1,0 +1,169 @@
+// Shared device helpers for the tpo_b200 kernels (sm_100a only).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/tpo_b200.h"
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
+#error "tpo_b200 kernels are written for sm_100a (B200) only"
+#endif
+
+namespace tpo {
+
+// ---------------------------------------------------------------------------
+// Packed fp32x2 arithmetic (sm_100: one instruction drives two FP32 lanes, so
+// the FP32 pipe can be saturated with half the issue slots).  Explicit .rn
+// rounding: IEEE per element, never contracted by ptxas.
+// ---------------------------------------------------------------------------
+typedef unsigned long long u64;
+
+__device__ __forceinline__ u64 pk(float lo, float hi) {
+  u64 r;
+  asm("mov.b64 %0, {%1,%2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void upk(u64 v, float& lo, float& hi) {
+  asm("mov.b64 {%0,%1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ u64 sub2(u64 a, u64 b) {
+  u64 r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ u64 mul2(u64 a, u64 b) {
+  u64 r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ u64 add2(u64 a, u64 b) {
+  u64 r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ u64 fma2(u64 a, u64 b, u64 c) {
+  u64 r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+
+// Squared distance of two packed lanes, in the reference's operation order.
+// MODE 0 (TPO_ROUND_FMA): fma(dz,dz, fma(dy,dy, dx*dx)); MODE 1: (dx*dx+dy*dy)+dz*dz.
+template <int MODE>
+__device__ __forceinline__ u64 dist2x2(u64 dx, u64 dy, u64 dz) {
+  if (MODE == TPO_ROUND_FMA) {
+    u64 t = mul2(dx, dx);
+    t = fma2(dy, dy, t);
+    return fma2(dz, dz, t);
+  } else {
+    u64 t = mul2(dx, dx);
+    t = add2(t, mul2(dy, dy));
+    return add2(t, mul2(dz, dz));
+  }
+}
+
+// Scalar forms with the same rounding (used by the finalize rescans).
+template <int MODE>
+__device__ __forceinline__ float dist1f(float dx, float dy, float dz) {
+  if (MODE == TPO_ROUND_FMA) {
+    return __fmaf_rn(dz, dz, __fmaf_rn(dy, dy, __fmul_rn(dx, dx)));
+  } else {
+    return __fadd_rn(__fadd_rn(__fmul_rn(dx, dx), __fmul_rn(dy, dy)), __fmul_rn(dz, dz));
+  }
+}
+template <int MODE>
+__device__ __forceinline__ double dist1d(double dx, double dy, double dz) {
+  if (MODE == TPO_ROUND_FMA) {
+    return __fma_rn(dz, dz, __fma_rn(dy, dy, __dmul_rn(dx, dx)));
+  } else {
+    return __dadd_rn(__dadd_rn(__dmul_rn(dx, dx), __dmul_rn(dy, dy)), __dmul_rn(dz, dz));
+  }
+}
+
+// fp16 with c10::Half semantics: every operation rounds to half (RN), nothing fused.
+__device__ __forceinline__ __half hsub_rn(__half a, __half b) {
+  __half r;
+  asm("sub.rn.f16 %0, %1, %2;" : "=h"(*reinterpret_cast<unsigned short*>(&r))
+      : "h"(*reinterpret_cast<unsigned short*>(&a)), "h"(*reinterpret_cast<unsigned short*>(&b)));
+  return r;
+}
+__device__ __forceinline__ __half hmul_rn(__half a, __half b) {
+  __half r;
+  asm("mul.rn.f16 %0, %1, %2;" : "=h"(*reinterpret_cast<unsigned short*>(&r))
+      : "h"(*reinterpret_cast<unsigned short*>(&a)), "h"(*reinterpret_cast<unsigned short*>(&b)));
+  return r;
+}
+__device__ __forceinline__ __half hadd_rn(__half a, __half b) {
+  __half r;
+  asm("add.rn.f16 %0, %1, %2;" : "=h"(*reinterpret_cast<unsigned short*>(&r))
+      : "h"(*reinterpret_cast<unsigned short*>(&a)), "h"(*reinterpret_cast<unsigned short*>(&b)));
+  return r;
+}
+// (dx*dx + dy*dy) + dz*dz, each op rounded to half; chamfer.cu:64-67 with c10::Half.
+__device__ __forceinline__ __half dist1h(__half dx, __half dy, __half dz) {
+  return hadd_rn(hadd_rn(hmul_rn(dx, dx), hmul_rn(dy, dy)), hmul_rn(dz, dz));
+}
+
+__device__ __forceinline__ float min3f(float a, float b, float c) {
+  float r;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+__device__ __forceinline__ unsigned redux_min_u32(unsigned v) {
+  unsigned r;
+  asm volatile("redux.sync.min.u32 %0, %1, 0xffffffff;" : "=r"(r) : "r"(v));
+  return r;
+}
+
+// Fire-and-forget global atomic min on a packed 64-bit key.
+__device__ __forceinline__ void red_min_u64(u64* addr, u64 v) {
+  asm volatile("red.relaxed.gpu.global.min.u64 [%0], %1;" ::"l"(addr), "l"(v) : "memory");
+}
+
+// 128-bit key {lo = chunk index, hi = distance bits} for fp64: lexicographic min
+// via a 16-byte compare-and-swap loop (atom.cas.b128, sm_90+).
+struct alignas(16) Key128 {
+  u64 lo, hi;
+};
+__device__ __forceinline__ bool key128_less(u64 ahi, u64 alo, u64 bhi, u64 blo) {
+  return ahi < bhi || (ahi == bhi && alo < blo);
+}
+__device__ __forceinline__ void cas128(Key128* addr, u64 cmp_lo, u64 cmp_hi, u64 new_lo,
+                                       u64 new_hi, u64& old_lo, u64& old_hi) {
+  asm volatile(
+      "{\n\t.reg .b128 c, n, o;\n\t"
+      "mov.b128 c, {%2, %3};\n\t"
+      "mov.b128 n, {%4, %5};\n\t"
+      "atom.relaxed.gpu.global.cas.b128 o, [%6], c, n;\n\t"
+      "mov.b128 {%0, %1}, o;\n\t}"
+      : "=l"(old_lo), "=l"(old_hi)
+      : "l"(cmp_lo), "l"(cmp_hi), "l"(new_lo), "l"(new_hi), "l"(addr)
+      : "memory");
+}
+__device__ __forceinline__ void key128_min(Key128* addr, u64 hi, u64 lo) {
+  u64 cur_lo = addr->lo, cur_hi = addr->hi;  // a torn read only costs an extra CAS round
+  // Bounded: every failed CAS means another thread stored a strictly smaller key,
+  // which can happen at most once per competing writer.
+  for (int it = 0; it < (1 << 20); ++it) {
+    if (!key128_less(hi, lo, cur_hi, cur_lo)) return;
+    u64 o_lo, o_hi;
+    cas128(addr, cur_lo, cur_hi, lo, hi, o_lo, o_hi);
+    if (o_lo == cur_lo && o_hi == cur_hi) return;
+    cur_lo = o_lo;
+    cur_hi = o_hi;
+  }
+}
+
+__host__ __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
+__host__ __device__ __forceinline__ int64_t max64(int64_t a, int64_t b) { return a > b ? a : b; }
+
+__device__ __forceinline__ unsigned lane_id() {
+  unsigned r;
+  asm("mov.u32 %0, %%laneid;" : "=r"(r));
+  return r;
+}
+
+}  // namespace tpo

@@ -1,0 +1,42 @@
+// Internal declarations shared by the tpo_b200 translation units.
+#pragma once
+
+#include <algorithm>
+#include <cstdint>
+
+#include "tpo_common.cuh"
+
+namespace tpo {
+
+// Records the CUDA error text for tpo_status_string and maps it to TPO_ERR_CUDA.
+int cuda_status(cudaError_t e);
+// cudaGetLastError() after a launch.
+int check_launch();
+
+int chamfer_fwd_keys(int dtype, int flags, const void* x1, const void* x2, int64_t B, int64_t N,
+                     int64_t M, int64_t rb0, int64_t rb1, void* k1, void* k2, cudaStream_t st);
+int chamfer_finalize(int dtype, int flags, const void* x1, const void* x2, int64_t B, int64_t N,
+                     int64_t M, int64_t rb0, int64_t rb1, const void* k1, const void* k2, void* d1,
+                     int32_t* i1, void* d2, int32_t* i2, cudaStream_t st);
+int chamfer_bwd_accumulate(int dtype, const void* x1, const void* x2, int64_t B, int64_t N,
+                           int64_t M, int64_t r0, int64_t r1, int64_t c0, int64_t c1,
+                           const int32_t* i1, const int32_t* i2, const void* g1, const void* g2,
+                           void* gx1, void* gx2, cudaStream_t st);
+int knn_forward(int dtype, int flags, const void* p1, const void* p2, const int64_t* l1,
+                const int64_t* l2, int64_t N, int64_t P1, int64_t P2, int64_t D, int64_t norm,
+                int64_t K, void* dists, int64_t* idxs, cudaStream_t st);
+int knn_backward(int dtype, const void* p1, const void* p2, const int64_t* l1, const int64_t* l2,
+                 const int64_t* idxs, int64_t N, int64_t P1, int64_t P2, int64_t D, int64_t K,
+                 int64_t norm, const void* gd, void* g1, void* g2, cudaStream_t st);
+int knn_gather_forward(int dtype, const void* x, const int64_t* idx, const int64_t* lengths,
+                       int64_t N, int64_t M, int64_t U, int64_t L, int64_t K, void* out,
+                       cudaStream_t st);
+int knn_gather_backward(int dtype, const void* gout, const int64_t* idx, const int64_t* lengths,
+                        int64_t N, int64_t M, int64_t U, int64_t L, int64_t K, void* gx,
+                        cudaStream_t st);
+
+inline int dtype_size(int dtype) {
+  return dtype == TPO_F32 ? 4 : dtype == TPO_F16 ? 2 : dtype == TPO_F64 ? 8 : 0;
+}
+
+}  // namespace tpo
