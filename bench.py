@@ -1,0 +1,527 @@
+"""Benchmark: Chamfer fwd+bwd in G point-pairs/s on B200 (one process per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2|2h|3|4|5|5d]
+                    [--impl ours|reference]
+
+A step = one forward + backward pass of the chamfer (or knn) path over one batch
+of seeded synthetic input with the benchmark configuration's shapes and
+distributions.  Default workload: configuration 2 (B=32, N=M=2048, fp32, unit
+sphere + N(0, 0.01^2) noise), the configuration the headline metric is quoted on.
+
+Timing: W untimed warm-up steps, then K timed steps, each bracketed by CUDA
+events on the launching stream; a 256 MiB buffer (> 126 MB L2) is rewritten
+before every timed step so no step starts with a warm L2.  Multi-GPU: each rank
+runs its own batch (weak scaling, no data-path collective), a barrier +
+synchronize brackets the timed region and the per-rank device time is
+max-reduced.  Rank 0 prints one JSON line.
+
+`value` = device-resident throughput (inputs already in HBM; the step is a CUDA
+graph of the public API's forward + backward).  `e2e` = the same metric through
+the public API (ChamferDistance / knn_points) with pinned HOST inputs: H2D copy,
+forward, backward and D2H of loss + gradients inside the timed region.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "tests"))
+
+SMS = 148
+FP32_LANES = 128
+MAX_SM_MHZ = 1965.0
+INSTR_PER_PAIR = 6  # 3 FADD + 1 FMUL + 2 FFMA (the reference's 8 FLOPs/pair)
+
+CONFIGS = {
+    "2": dict(kind="chamfer", B=32, N=2048, M=2048, dtype="float32", gen="sphere",
+              desc="Chamfer fwd+bwd B=32 N=M=2048 fp32 sphere+noise (config 2)"),
+    "2h": dict(kind="chamfer", B=32, N=2048, M=2048, dtype="float16", gen="sphere",
+               desc="Chamfer fwd+bwd B=32 N=M=2048 fp16 sphere+noise (config 2, fp16)"),
+    "1": dict(kind="chamfer", B=4, N=1024, M=1024, dtype="float32", gen="uniform",
+              desc="Chamfer fwd+bwd B=4 N=M=1024 fp32 uniform (config 1)"),
+    "3": dict(kind="chamfer", B=16, N=16384, M=8192, dtype="float32", gen="gmm",
+              desc="Chamfer fwd+bwd B=16 N=16384 M=8192 fp32 GMM (config 3)"),
+    "4": dict(kind="knn", B=8, N=8192, M=8192, K=16, dtype="float32", gen="knn4",
+              desc="knn_points fwd+bwd K=16 B=8 P=8192 ragged, return_nn (config 4)"),
+    "5": dict(kind="chamfer", B=1, N=1 << 20, M=1 << 20, dtype="float32", gen="lidar",
+              desc="Chamfer fwd+bwd B=1 N=M=2^20 fp32 LiDAR-like (config 5)"),
+    "5d": dict(kind="chamfer", B=1, N=1 << 20, M=1 << 20, dtype="float64", gen="lidar",
+               desc="Chamfer fwd+bwd B=1 N=M=2^20 fp64 LiDAR-like (config 5, fp64)"),
+}
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown," \
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown," \
+             "clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in self.lines:
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[4:8]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": MAX_SM_MHZ, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def make_inputs(cfg, seed):
+    import datagen
+
+    dt = getattr(torch, cfg["dtype"])
+    g = cfg["gen"]
+    B, N, M = cfg["B"], cfg["N"], cfg["M"]
+    if g == "sphere":
+        return datagen.sphere_noise(B, N, seed, dtype=dt), datagen.sphere_noise(B, M, seed + 1, dtype=dt)
+    if g == "uniform":
+        return datagen.uniform(B, N, seed, dtype=dt), datagen.uniform(B, M, seed + 1, dtype=dt)
+    if g == "gmm":
+        return datagen.gmm(B, N, seed, dtype=dt), datagen.gmm(B, M, seed + 1, dtype=dt)
+    if g == "lidar":
+        return datagen.lidar(N, seed, dtype=dt), datagen.lidar(M, seed + 1, dtype=dt)
+    if g == "knn4":
+        return datagen.knn_config4(seed, dtype=dt, B=B, P=N)
+    raise ValueError(g)
+
+
+def pairs_of(cfg, inputs):
+    if cfg["kind"] == "knn":
+        _, _, l1, l2 = inputs
+        return int((l1.long() * l2.long()).sum())
+    return cfg["B"] * cfg["N"] * cfg["M"]
+
+
+# ----------------------------------------------------------------- our arm ----
+def step_fn(cfg):
+    import torch_point_ops_b200 as tpo
+
+    if cfg["kind"] == "chamfer":
+        crit = tpo.ChamferDistance("mean")
+
+        def step(x1, x2):
+            loss = crit(x1, x2)
+            g1, g2 = torch.autograd.grad(loss, [x1, x2])
+            return loss, g1, g2
+        return step
+    knn = tpo.KNearestNeighbors(K=cfg["K"], return_nn=True)
+
+    def kstep(p1, p2, l1, l2):
+        _, dists, nn = knn(p1, p2, l1, l2)
+        loss = dists.sum() + nn.sum()
+        g1, g2 = torch.autograd.grad(loss, [p1, p2])
+        return loss, g1, g2
+    return kstep
+
+
+def launches_per_step(cfg):
+    # chamfer: keys + finalize (fwd), scatter (bwd); knn: knn fwd, gather fwd,
+    # gather bwd, knn bwd
+    return 3 if cfg["kind"] == "chamfer" else 4
+
+
+def run_ours(args, cfg):
+    import torch_point_ops_b200 as tpo  # noqa: F401
+
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
+    host_inputs = make_inputs(cfg, seed=1000 + 17 * rank)
+    pairs = pairs_of(cfg, host_inputs)
+    inputs = [t.to(dev) for t in host_inputs]
+    diff = [t.requires_grad_() if t.is_floating_point() else t for t in inputs]
+    step = step_fn(cfg)
+    flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)  # 256 MiB > L2
+
+    # ---- device-resident path: the step captured as a CUDA graph ----
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(max(3, args.warmup)):
+            out = step(*diff)
+    torch.cuda.current_stream().wait_stream(s)
+    graph = None
+    try:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            out = step(*diff)
+    except Exception as e:  # capture unsupported -> eager (reported)
+        graph = None
+        print(f"[bench] graph capture failed ({e}); timing eager steps", file=sys.stderr)
+
+    def run_step():
+        if graph is not None:
+            graph.replay()
+        else:
+            step(*diff)
+
+    for _ in range(args.warmup):
+        run_step()
+    torch.cuda.synchronize()
+    if ws > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            flush.fill_(float(i))
+            ev[i][0].record()
+            run_step()
+            ev[i][1].record()
+        torch.cuda.synchronize()
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+    total_ms = sum(step_ms)
+    if ws > 1:
+        torch.distributed.barrier()
+        t = torch.tensor([total_ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        total_ms = float(t.item())
+    ms_per_step = total_ms / args.steps
+    value = pairs * ws * args.steps / (total_ms * 1e-3) / 1e9
+
+    # ---- e2e through the public API with pinned host buffers ----
+    e2e = run_e2e(args, cfg, step, host_inputs, dev, flush, ws)
+    e2e_value = pairs * ws / (e2e["ms"] * 1e-3) / 1e9
+
+    # ---- the dominant kernel alone, for the roofline ----
+    roof = kernel_roofline(cfg, inputs, dev, clk.summary())
+    return dict(value=value, ms_per_step=ms_per_step, pairs=pairs, graph=graph is not None,
+                clocks=clk.summary(), e2e=e2e, e2e_value=e2e_value, roofline=roof)
+
+
+def run_e2e(args, cfg, step, host_inputs, dev, flush, ws):
+    pinned = [t.pin_memory() for t in host_inputs]
+    hi_bytes = sum(t.numel() * t.element_size() for t in pinned)
+    outs_host = None
+
+    def once():
+        nonlocal outs_host
+        xs = [t.to(dev, non_blocking=True) for t in pinned]
+        xs = [t.requires_grad_() if t.is_floating_point() else t for t in xs]
+        loss, g1, g2 = step(*xs)
+        outs = [loss.detach(), g1, g2]
+        if outs_host is None:
+            outs_host = [torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in outs]
+        for h, o in zip(outs_host, outs):
+            h.copy_(o, non_blocking=True)
+    for _ in range(max(3, args.warmup)):
+        once()
+    torch.cuda.synchronize()
+    if ws > 1:
+        torch.distributed.barrier()
+    tot = 0.0
+    for i in range(args.steps):
+        flush.fill_(float(i))
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        once()
+        b.record()
+        b.synchronize()
+        tot += a.elapsed_time(b)
+    if ws > 1:
+        t = torch.tensor([tot], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        tot = float(t.item())
+    bo = sum(h.numel() * h.element_size() for h in outs_host)
+    return {"ms": tot / args.steps, "h2d": hi_bytes, "d2h": bo}
+
+
+def kernel_roofline(cfg, inputs, dev, clocks, reps=20):
+    """Times the dominant kernel alone (CUDA events on its launching stream) and
+    reports achieved pair throughput against the FP32-pipe roofline."""
+    import torch_point_ops_b200 as tpo
+
+    if cfg["kind"] != "chamfer" or cfg["dtype"] != "float32":
+        return None
+    ops = tpo._lib.chamfer_ops
+    x1, x2 = [t.detach().contiguous() for t in inputs[:2]]
+    B, N, M = x1.shape[0], x1.shape[1], x2.shape[1]
+    k1 = ops.chamfer_keys_empty(x1, B * N)
+    k2 = ops.chamfer_keys_empty(x1, B * M)
+    for _ in range(3):
+        ops.chamfer_fwd_keys(x1, x2, 0, N, 0, k1, k2)
+    flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)
+    tot = 0.0
+    for i in range(reps):
+        flush.fill_(float(i))
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        ops.chamfer_fwd_keys(x1, x2, 0, N, 0, k1, k2)
+        b.record()
+        b.synchronize()
+        tot += a.elapsed_time(b)
+    ms = tot / reps
+    pairs = B * N * M
+    achieved = pairs / (ms * 1e-3) / 1e9
+    peak = SMS * FP32_LANES * MAX_SM_MHZ * 1e6 / INSTR_PER_PAIR / 1e9
+    out = {"bound": "fp32", "kernel": "chamfer_keys_f32_kernel", "achieved": round(achieved, 1),
+           "peak": round(peak, 1), "unit": "Gpair/s", "frac": round(achieved / peak, 4),
+           "peak_basis": "nominal FP32 pipe: 148 SM x 128 lanes x 1965 MHz / 6 instr per pair "
+                         "(MEASURED_PEAKS.json has no FP32 figure)",
+           "kernel_ms": round(ms, 4), "traffic": None}
+    if clocks.get("sm_mhz"):
+        p2 = SMS * FP32_LANES * clocks["sm_mhz"] * 1e6 / INSTR_PER_PAIR / 1e9
+        out["frac_at_measured_clock"] = round(achieved / p2, 4)
+    return out
+
+
+# ------------------------------------------------------ CPU reference path ----
+def cpu_reference_ops():
+    """The reference's own CPU knn operator built from its sources (oracle/_ref)
+    when present ('reference'), else the C restatement ('port')."""
+    import oracle
+
+    ops = oracle.ref_knn()
+    return ("reference", ops) if ops is not None else ("port", None)
+
+
+def cpu_chamfer_sample(cfg, host_inputs, max_rows=None, threads=None):
+    """Chamfer fwd+bwd on the CPU path of the reference: knn(K=1) in both
+    directions + knn_backward (chamfer has no CPU kernel, chamfer.cpp:21-24),
+    batches spread over host threads.  Returns (unordered pairs done, seconds,
+    kind, cores, sample description)."""
+    import concurrent.futures as cf
+
+    import numpy as np
+    import oracle
+
+    kind, ops = cpu_reference_ops()
+    threads = threads or os.cpu_count() or 1
+    x1, x2 = host_inputs[:2]
+    B, N, M = x1.shape[0], x1.shape[1], x2.shape[1]
+    rows = N if max_rows is None else min(N, max_rows)
+    per_b = max(1, -(-threads // B))
+    chunk = max(1, -(-rows // per_b))
+    tasks = [(b, r0, min(rows, r0 + chunk)) for b in range(B) for r0 in range(0, rows, chunk)]
+
+    def work(t):
+        b, r0, r1 = t
+        a = x1[b:b + 1, r0:r1].contiguous()
+        c = x2[b:b + 1, r0:r1].contiguous()
+        if ops is not None:
+            la, lc = torch.tensor([r1 - r0]), torch.tensor([r1 - r0])
+            fa, fc = torch.tensor([M]), torch.tensor([N])
+            i1, _ = ops.knn_forward(a, x2[b:b + 1], la, fa, 2, 1, -1)
+            i2, _ = ops.knn_forward(c, x1[b:b + 1], lc, fc, 2, 1, -1)
+            g = torch.ones(1, r1 - r0, 1, dtype=a.dtype)
+            ops.knn_backward(a, x2[b:b + 1], la, fa, i1, 2, g)
+            ops.knn_backward(c, x1[b:b + 1], lc, fc, i2, 2, g)
+        else:
+            oracle.nn(a.numpy(), x2[b:b + 1].numpy(), 0)
+            oracle.nn(c.numpy(), x1[b:b + 1].numpy(), 0)
+
+    t0 = time.perf_counter()
+    if ops is not None:
+        with cf.ThreadPoolExecutor(threads) as ex:
+            list(ex.map(work, tasks))
+        cores = threads
+    else:
+        for t in tasks:
+            work(t)
+        cores = threads  # the C oracle uses OpenMP over all host threads
+    dt = time.perf_counter() - t0
+    done = B * rows * (M + N) / 2  # unordered-pair equivalents (each direction = half)
+    sample = (f"{B} batch(es) x {rows} of {N} rows per direction, K=1 knn_forward both "
+              f"directions + knn_backward, {threads} threads")
+    return done, dt, kind, cores, sample
+
+
+def cpu_knn_sample(cfg, host_inputs, max_rows=256, threads=None):
+    import concurrent.futures as cf
+
+    import numpy as np
+    import oracle
+
+    kind, ops = cpu_reference_ops()
+    threads = threads or os.cpu_count() or 1
+    p1, p2, l1, l2 = host_inputs
+    B = p1.shape[0]
+    K = cfg["K"]
+    tasks = [(b, r0) for b in range(B) for r0 in range(0, max_rows, 32)]
+
+    def work(t):
+        b, r0 = t
+        r1 = min(int(l1[b]), r0 + 32)
+        if r1 <= r0:
+            return 0
+        q = p1[b:b + 1, r0:r1].contiguous()
+        ll1 = torch.tensor([r1 - r0])
+        ll2 = l2[b:b + 1]
+        if ops is not None:
+            i, d = ops.knn_forward(q, p2[b:b + 1], ll1, ll2, 2, K, -1)
+            ops.knn_backward(q, p2[b:b + 1], ll1, ll2, i, 2, torch.ones_like(d))
+        else:
+            oracle.knn_fwd(q.numpy(), p2[b:b + 1].numpy(), ll1.numpy(), ll2.numpy(), 2, K, 0)
+        return (r1 - r0) * int(l2[b])
+
+    t0 = time.perf_counter()
+    with cf.ThreadPoolExecutor(threads if ops is not None else 1) as ex:
+        done = sum(ex.map(work, tasks))
+    dt = time.perf_counter() - t0
+    return done, dt, kind, threads, f"{B} batches x first {max_rows} valid query rows, K={K} knn fwd+bwd, {threads} threads"
+
+
+def cpu_measure(cfg, host_inputs, budget_s=15.0):
+    """Bounded CPU sample (~budget_s); returns the cpu_baseline object."""
+    if cfg["kind"] == "knn":
+        done, dt, kind, cores, sample = cpu_knn_sample(cfg, host_inputs)
+    else:
+        N = cfg["N"]
+        rows = N
+        # shrink rows so one sample takes about budget_s / 3 seconds
+        probe_rows = min(N, 64)
+        done, dt, kind, cores, sample = cpu_chamfer_sample(cfg, host_inputs, max_rows=probe_rows)
+        rate = done / max(dt, 1e-6)
+        want = rate * budget_s / 3
+        rows = int(min(N, max(probe_rows, want * 2 / (cfg["B"] * (cfg["N"] + cfg["M"])))))
+        done, dt, kind, cores, sample = cpu_chamfer_sample(cfg, host_inputs, max_rows=rows)
+    return {"value": round(done / dt / 1e9, 4), "unit": "Gpair/s", "cores": cores, "kind": kind,
+            "sample": sample, "seconds": round(dt, 3)}
+
+
+def run_reference(args, cfg):
+    """Reference arm: the reference's own CPU implementation of the path on this
+    host's cores (the reference chamfer has no CPU kernel; its CPU path is knn K=1
+    both ways + knn_backward).  Rank 0 only; other ranks exit without work."""
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return None
+    host_inputs = make_inputs(cfg, seed=1000)
+    vals = []
+    last = None
+    for i in range(args.warmup + args.steps):
+        last = cpu_measure(cfg, host_inputs, budget_s=max(3.0, 60.0 / max(1, args.steps + args.warmup)))
+        if i >= args.warmup:
+            vals.append(last["value"])
+    v = statistics.median(vals)
+    pairs = pairs_of(cfg, host_inputs)
+    line = {
+        "impl": "reference", "metric": "Chamfer fwd+bwd G point-pairs/s" if cfg["kind"] == "chamfer"
+        else "knn_points fwd+bwd G point-pairs/s", "value": v, "unit": "Gpair/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(pairs / (v * 1e9) * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": cfg["dtype"].replace("float", "f"),
+        "data": "synthetic (seeded, config distribution)",
+        "config": {"workload": cfg["desc"]},
+        "cpu_baseline": {k: last[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": v, "unit": "Gpair/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    line["cpu_baseline"]["value"] = v
+    return line
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="2", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    cfg = CONFIGS[args.config]
+    ws, rank, _ = dist_env()
+
+    if args.impl == "reference":
+        line = run_reference(args, cfg)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+
+    r = run_ours(args, cfg)
+    if rank != 0:
+        torch.distributed.destroy_process_group() if ws > 1 else None
+        return
+    cpu = None
+    if not args.no_cpu and ws == 1:
+        cpu = cpu_measure(cfg, make_inputs(cfg, seed=1000), budget_s=15.0)
+        cpu = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    line = {
+        "metric": "Chamfer fwd+bwd G point-pairs/s" if cfg["kind"] == "chamfer"
+        else "knn_points fwd+bwd G point-pairs/s",
+        "value": round(r["value"], 2), "unit": "Gpair/s", "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(r["ms_per_step"], 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": cfg["dtype"].replace("float", "f"),
+        "data": "synthetic (seeded, config distribution)",
+        "config": {"workload": cfg["desc"], "pairs_per_step_per_gpu": r["pairs"],
+                   "l2": "256 MiB buffer rewritten before every timed step",
+                   "parallelism": f"dp{ws} (independent batch per GPU)",
+                   "cuda_graph": r["graph"]},
+        "clocks": r["clocks"],
+        "e2e": {"value": round(r["e2e_value"], 2), "unit": "Gpair/s",
+                "h2d_bytes_per_step": r["e2e"]["h2d"], "d2h_bytes_per_step": r["e2e"]["d2h"],
+                "ms_per_step": round(r["e2e"]["ms"], 4)},
+        "gpu_launches": launches_per_step(cfg) * args.steps,
+        "roofline": r["roofline"],
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+    if ws > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
