@@ -223,13 +223,24 @@ def run_ours(args, cfg):
         torch.distributed.barrier()
     torch.cuda.synchronize()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+
+    def load(seconds):
+        # untimed replays so nvidia-smi (100 ms sampling) sees the GPU under this load
+        t0 = time.perf_counter()
+        while time.perf_counter() - t0 < seconds:
+            for _ in range(20):
+                run_step()
+            torch.cuda.synchronize()
+
     with ClockSampler(local) as clk:
+        load(1.0)
         for i in range(args.steps):
             flush.fill_(float(i))
             ev[i][0].record()
             run_step()
             ev[i][1].record()
         torch.cuda.synchronize()
+        load(0.5)
     step_ms = [a.elapsed_time(b) for a, b in ev]
     total_ms = sum(step_ms)
     if ws > 1:

@@ -33,12 +33,15 @@ extern "C" {
 /* element types (match torch's float32 / float16 / float64) */
 enum tpo_dtype { TPO_F32 = 0, TPO_F16 = 1, TPO_F64 = 2 };
 
-/* flags for the distance arithmetic.
- * TPO_ROUND_FMA (default, 0): d = fma(dz,dz, fma(dy,dy, dx*dx)) -- the rounding of
- *   the reference CUDA kernels (nvcc contracts chamfer.cu:67 and knn.cu:154).
+/* flags for the chamfer distance arithmetic.
+ * TPO_ROUND_FMA (default, 0): d = fma(dz,dz, fma(dx,dx, dy*dy)) -- bit-identical to
+ *   the reference CUDA chamfer kernel (nvcc's contraction of chamfer.cu:67,
+ *   measured on B200).
  * TPO_ROUND_EXACT: d = (dx*dx + dy*dy) + dz*dz with every operation rounded --
  *   the rounding of the reference CPU path (knn.cpp:64-72).
- * fp16 always rounds every operation (c10::Half semantics); the flag is ignored. */
+ * knn ignores the flag: the reference knn CUDA kernels are not contracted
+ *   (measured), so both reference knn paths round like TPO_ROUND_EXACT.
+ * fp16 always rounds every operation (c10::Half semantics). */
 enum tpo_flags { TPO_ROUND_FMA = 0, TPO_ROUND_EXACT = 1 };
 
 enum tpo_status {

@@ -28,10 +28,13 @@
  * Rounding modes (`mode`):
  *   0  "exact": every product and sum rounded separately, no contraction.
  *      This is the reference CPU path (g++ -O3 on x86-64 baseline emits no FMA).
- *   1  "fma":  t = dx*dx; t = fma(dy,dy,t); t = fma(dz,dz,t) -- the contraction
- *      nvcc applies to the reference CUDA kernels (default --fmad=true; the
- *      reference's setup.py:83-92 does not override it).  Pinned against the
- *      reference CUDA build by tests/test_ref_cuda_pin.py on the GPU box.
+ *   1  "fma":  t = dy*dy; t = fma(dx,dx,t); t = fma(dz,dz,t) -- the contraction
+ *      nvcc applies to the reference CUDA chamfer kernel's x2*x2+y2*y2+z2*z2
+ *      (chamfer.cu:67; default --fmad=true, setup.py:83-92 does not override it).
+ *      Determined by comparing the reference CUDA build's outputs on a B200 with
+ *      candidate orders (it matches this one bit for bit) and pinned by
+ *      tests/test_ref_cuda_pin.py.  The reference CUDA knn kernels are NOT
+ *      contracted (their outputs equal mode 0), so knn always uses mode 0.
  * fp16 follows c10::Half: every sub/mul/add rounds to half (round-to-nearest-
  * even), no fused operations, in both modes.
  *
@@ -46,13 +49,13 @@ typedef _Float16 h16;
 
 /* ---------------- distance kernels ---------------- */
 static inline float d2_f32(int mode, float dx, float dy, float dz) {
-  if (mode == 1) return fmaf(dz, dz, fmaf(dy, dy, dx * dx));
+  if (mode == 1) return fmaf(dz, dz, fmaf(dx, dx, dy * dy));
   float t = dx * dx;
   t = t + dy * dy;
   return t + dz * dz;
 }
 static inline double d2_f64(int mode, double dx, double dy, double dz) {
-  if (mode == 1) return fma(dz, dz, fma(dy, dy, dx * dx));
+  if (mode == 1) return fma(dz, dz, fma(dx, dx, dy * dy));
   double t = dx * dx;
   t = t + dy * dy;
   return t + dz * dz;

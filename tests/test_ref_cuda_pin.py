@@ -2,8 +2,9 @@
 
 oracle/_ref holds the reference chamfer/knn sources compiled unmodified with the
 flags of the reference's setup.py (oracle/Makefile.ref).  On the GPU this checks
-that (a) the reference CUDA distances equal the oracle's "fma" mode bit for bit
--- i.e. nvcc contracts dx*dx+dy*dy+dz*dz into fma(dz,dz,fma(dy,dy,dx*dx)) --
+that (a) the reference CUDA chamfer distances equal the oracle's "fma" mode bit for
+bit -- nvcc contracts x2*x2+y2*y2+z2*z2 into fma(dz,dz,fma(dx,dx,dy*dy)) -- and
+the reference CUDA knn distances equal the uncontracted mode,
 and (b) this library's default output equals the reference CUDA output.
 Skipped when oracle/_ref was not built."""
 import numpy as np
@@ -52,7 +53,7 @@ def test_reference_knn_cuda_rounding(dtype):
     # the reference sorts in Python (knn/__init__.py:130-131)
     rd, order = rd.sort(dim=2)
     ri = ri.gather(2, order)
-    oi, od = oracle.knn_fwd(p1.numpy(), p2.numpy(), L1.numpy(), L2.numpy(), 2, 16, 1)
+    oi, od = oracle.knn_fwd(p1.numpy(), p2.numpy(), L1.numpy(), L2.numpy(), 2, 16, 0)
     assert np.array_equal(_bits(rd), od.view(np.uint8))
     assert np.array_equal(ri.cpu().numpy(), oi)
     i, d = C.knn_fwd(p1.cuda(), p2.cuda(), L1.cuda(), L2.cuda(), 2, 16, 0)

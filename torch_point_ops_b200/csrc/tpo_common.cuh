@@ -50,17 +50,26 @@ __device__ __forceinline__ u64 fma2(u64 a, u64 b, u64 c) {
 }
 
 // Squared distance of two packed lanes, in the reference's operation order.
-// MODE 0 (TPO_ROUND_FMA): fma(dz,dz, fma(dy,dy, dx*dx)); MODE 1: (dx*dx+dy*dy)+dz*dz.
+// MODE 0 (TPO_ROUND_FMA): fma(dz,dz, fma(dx,dx, dy*dy)) -- bit-identical to the
+// reference CUDA chamfer kernel as nvcc contracts it (measured on B200);
+// MODE 1 (TPO_ROUND_EXACT): (dx*dx + dy*dy) + dz*dz, every operation rounded.
 template <int MODE>
 __device__ __forceinline__ u64 dist2x2(u64 dx, u64 dy, u64 dz) {
   if (MODE == TPO_ROUND_FMA) {
-    u64 t = mul2(dx, dx);
-    t = fma2(dy, dy, t);
+    u64 t = mul2(dy, dy);
+    t = fma2(dx, dx, t);
     return fma2(dz, dz, t);
   } else {
-    u64 t = mul2(dx, dx);
-    t = add2(t, mul2(dy, dy));
-    return add2(t, mul2(dz, dz));
+    // Scalar .rn mul/add: PTX guarantees these are never fused.  (Measured on
+    // B200: ptxas may fuse a mul.rn.f32x2 + add.rn.f32x2 pair into an FMA, which
+    // would silently turn this mode into the FMA rounding.)
+    float x0, x1, y0, y1, z0, z1;
+    upk(dx, x0, x1);
+    upk(dy, y0, y1);
+    upk(dz, z0, z1);
+    const float r0 = __fadd_rn(__fadd_rn(__fmul_rn(x0, x0), __fmul_rn(y0, y0)), __fmul_rn(z0, z0));
+    const float r1 = __fadd_rn(__fadd_rn(__fmul_rn(x1, x1), __fmul_rn(y1, y1)), __fmul_rn(z1, z1));
+    return pk(r0, r1);
   }
 }
 
@@ -68,7 +77,7 @@ __device__ __forceinline__ u64 dist2x2(u64 dx, u64 dy, u64 dz) {
 template <int MODE>
 __device__ __forceinline__ float dist1f(float dx, float dy, float dz) {
   if (MODE == TPO_ROUND_FMA) {
-    return __fmaf_rn(dz, dz, __fmaf_rn(dy, dy, __fmul_rn(dx, dx)));
+    return __fmaf_rn(dz, dz, __fmaf_rn(dx, dx, __fmul_rn(dy, dy)));
   } else {
     return __fadd_rn(__fadd_rn(__fmul_rn(dx, dx), __fmul_rn(dy, dy)), __fmul_rn(dz, dz));
   }
@@ -76,7 +85,7 @@ __device__ __forceinline__ float dist1f(float dx, float dy, float dz) {
 template <int MODE>
 __device__ __forceinline__ double dist1d(double dx, double dy, double dz) {
   if (MODE == TPO_ROUND_FMA) {
-    return __fma_rn(dz, dz, __fma_rn(dy, dy, __dmul_rn(dx, dx)));
+    return __fma_rn(dz, dz, __fma_rn(dx, dx, __dmul_rn(dy, dy)));
   } else {
     return __dadd_rn(__dadd_rn(__dmul_rn(dx, dx), __dmul_rn(dy, dy)), __dmul_rn(dz, dz));
   }
