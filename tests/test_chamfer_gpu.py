@@ -186,3 +186,37 @@ def test_gradcheck_f64():
     x2 = torch.rand(1, 6, 3, generator=g, dtype=torch.float64).to(DEV).requires_grad_()
     assert torch.autograd.gradcheck(lambda a, b: tpo.chamfer_distance(a, b), (x1, x2),
                                     nondet_tol=1e-12)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float64, torch.float16])
+@pytest.mark.parametrize("reduction", [0, 1])
+def test_fused_loss_capi(dtype, reduction):
+    """tpo_chamfer_loss_fwd/bwd == chamfer_fwd + torch reduction + chamfer_bwd."""
+    x1 = datagen.sphere_noise(3, 1111, seed=8, dtype=dtype).to(DEV)
+    x2 = datagen.sphere_noise(3, 777, seed=9, dtype=dtype).to(DEV)
+    loss, i1, i2 = C.chamfer_loss_fwd(x1, x2, reduction)
+    d1, d2, j1, j2 = C.chamfer_fwd(x1, x2)
+    assert torch.equal(i1, j1) and torch.equal(i2, j2)
+    ref = (d1.mean() + d2.mean()) if reduction == 0 else (d1.sum() + d2.sum())
+    rtol = {torch.float32: 1e-5, torch.float64: 1e-12, torch.float16: 2e-3}[dtype]
+    assert torch.allclose(loss.double(), ref.double(), rtol=rtol), (loss, ref)
+    gl = torch.tensor([0.75], dtype=dtype, device=DEV)
+    gx1, gx2 = C.chamfer_loss_bwd(x1, x2, i1, i2, gl, reduction)
+    if reduction == 0:
+        g1 = (gl / d1.numel()).expand(d1.shape).contiguous()
+        g2 = (gl / d2.numel()).expand(d2.shape).contiguous()
+    else:
+        g1 = gl.expand(d1.shape).contiguous()
+        g2 = gl.expand(d2.shape).contiguous()
+    rx1, rx2 = C.chamfer_bwd(x1, x2, i1, i2, g1, g2)
+    atol = {torch.float32: 1e-7, torch.float64: 1e-15, torch.float16: 1e-3}[dtype]
+    assert torch.allclose(gx1.double(), rx1.double(), rtol=rtol, atol=atol * gl.item())
+    assert torch.allclose(gx2.double(), rx2.double(), rtol=rtol, atol=atol * gl.item())
+
+
+def test_fused_loss_two_calls_deterministic():
+    x1 = datagen.gmm(4, 3000, seed=3).to(DEV)
+    x2 = datagen.gmm(4, 2000, seed=4).to(DEV)
+    a = C.chamfer_loss_fwd(x1, x2)[0]
+    b = C.chamfer_loss_fwd(x1, x2)[0]
+    assert torch.equal(a, b)

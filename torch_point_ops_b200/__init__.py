@@ -5,12 +5,12 @@ names): ``import torch_point_ops_b200 as torch_point_ops``.
 """
 from . import _lib
 from ._lib import get_rounding, set_rounding
-from .chamfer import ChamferDistance, chamfer_distance, chamfer_distance_with_idx
+from .chamfer import ChamferDistance, chamfer_distance, chamfer_distance_with_idx, chamfer_loss
 from .knn import KNearestNeighbors, KNNFunction, knn_function, knn_gather, knn_points
 
 __version__ = "0.1.0"
 __all__ = [
-    "chamfer_distance", "chamfer_distance_with_idx", "ChamferDistance",
+    "chamfer_distance", "chamfer_distance_with_idx", "chamfer_loss", "ChamferDistance",
     "knn_points", "knn_gather", "KNearestNeighbors", "KNNFunction", "knn_function",
     "set_rounding", "get_rounding",
 ]

@@ -15,7 +15,7 @@ TORCH_BINDING_PATH = os.path.join(LIB_DIR, "libtpo_b200_torch.so")
 if not (os.path.exists(CAPI_PATH) and os.path.exists(TORCH_BINDING_PATH)):
     raise ImportError(
         "torch_point_ops_b200: native libraries not built; run "
-        "`python -m torch_point_ops_b200.build` (needs nvcc for sm_100a)")
+        "`python torch_point_ops_b200/build.py` (needs nvcc for sm_100a)")
 
 torch.ops.load_library(TORCH_BINDING_PATH)
 chamfer_ops = torch.ops.torch_point_ops_b200_chamfer

@@ -5,7 +5,8 @@ Produces, inside the package directory:
                            depends only on the CUDA driver (cudart linked statically).
   lib/libtpo_b200_torch.so torch.library binding over that C ABI.
 
-Usage:  python -m torch_point_ops_b200.build [--force]
+Usage:  python torch_point_ops_b200/build.py [--force]   (run as a script: importing
+        the package itself requires the built libraries)
 Incremental: a target is rebuilt when any of its sources or headers is newer.
 """
 from __future__ import annotations

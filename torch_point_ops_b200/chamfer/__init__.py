@@ -51,6 +51,45 @@ def _(xyz1, xyz2, idx1, idx2, grad_dist1, grad_dist2):
     return torch.empty_like(xyz1), torch.empty_like(xyz2)
 
 
+def _loss_setup(ctx, inputs, output):
+    xyz1, xyz2, reduction = inputs[0], inputs[1], inputs[2]
+    _, idx1, idx2 = output
+    ctx.save_for_backward(xyz1, xyz2, idx1, idx2)
+    ctx.reduction = reduction
+
+
+def _loss_backward(ctx, grad_loss, gi1, gi2):
+    xyz1, xyz2, idx1, idx2 = ctx.saved_tensors
+    gx1, gx2 = _ops.chamfer_loss_backward(xyz1, xyz2, idx1, idx2, grad_loss, ctx.reduction)
+    return gx1, gx2, None, None
+
+
+torch.library.register_autograd(
+    "torch_point_ops_b200_chamfer::chamfer_loss", _loss_backward, setup_context=_loss_setup)
+
+
+@torch.library.register_fake("torch_point_ops_b200_chamfer::chamfer_loss")
+def _(xyz1, xyz2, reduction, flags):
+    b, n, _ = xyz1.shape
+    m = xyz2.shape[1]
+    return (xyz1.new_empty(()), xyz1.new_empty(b, n, dtype=torch.int32),
+            xyz1.new_empty(b, m, dtype=torch.int32))
+
+
+@torch.library.register_fake("torch_point_ops_b200_chamfer::chamfer_loss_backward")
+def _(xyz1, xyz2, idx1, idx2, grad_loss, reduction):
+    return torch.empty_like(xyz1), torch.empty_like(xyz2)
+
+
+def chamfer_loss(xyz1: torch.Tensor, xyz2: torch.Tensor, reduction: str = "mean") -> torch.Tensor:
+    """Fused ChamferDistance loss: mean(dist1) + mean(dist2) ("mean") or
+    sum(dist1) + sum(dist2) ("sum"), computed inside the forward kernels (no
+    per-point distance tensors, no separate reduction launches); autograd-aware."""
+    red = {"mean": 0, "sum": 1}[reduction]
+    loss, _, _ = _ops.chamfer_loss(xyz1, xyz2, red, _lib.rounding_flags())
+    return loss
+
+
 def chamfer_distance(xyz1: torch.Tensor, xyz2: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """Chamfer distance between two point clouds.
 
@@ -79,4 +118,4 @@ def chamfer_distance_with_idx(xyz1, xyz2):
 
 from .chamfer import ChamferDistance  # noqa: E402
 
-__all__ = ["chamfer_distance", "chamfer_distance_with_idx", "ChamferDistance"]
+__all__ = ["chamfer_distance", "chamfer_distance_with_idx", "chamfer_loss", "ChamferDistance"]

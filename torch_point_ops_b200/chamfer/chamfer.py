@@ -1,7 +1,7 @@
 """ChamferDistance module -- drop-in for torch_point_ops/chamfer/chamfer.py:5-26."""
 import torch
 
-from . import chamfer_distance
+from . import chamfer_distance, chamfer_loss
 
 
 class ChamferDistance(torch.nn.Module):
@@ -19,9 +19,8 @@ class ChamferDistance(torch.nn.Module):
         self.reduction = reduction
 
     def forward(self, xyz1, xyz2):
-        dist1, dist2 = chamfer_distance(xyz1, xyz2)
-        if self.reduction == "mean":
-            return torch.mean(dist1) + torch.mean(dist2)
-        elif self.reduction == "sum":
-            return torch.sum(dist1) + torch.sum(dist2)
-        return dist1, dist2
+        # "mean"/"sum": one fused op (the reduction runs inside the finalize kernel
+        # and its gradient scaling inside the backward scatter)
+        if self.reduction in ("mean", "sum"):
+            return chamfer_loss(xyz1, xyz2, self.reduction)
+        return chamfer_distance(xyz1, xyz2)

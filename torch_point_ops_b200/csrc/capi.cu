@@ -100,7 +100,8 @@ int tpo_chamfer_finalize(int dtype, int flags, const void* xyz1, const void* xyz
   if (dist2 && B * M > 0 && (!idx2 || (N > 0 && !keys2)))
     return fail(TPO_ERR_INVALID_ARGUMENT, "chamfer: null column outputs");
   return chamfer_finalize(dtype, flags, xyz1, xyz2, B, N, M, row_begin, row_end, keys1, keys2,
-                          dist1, idx1, dist2, idx2, (cudaStream_t)stream);
+                          dist1, idx1, dist2, idx2, dist2 != nullptr, nullptr, 0, nullptr,
+                          (cudaStream_t)stream);
 }
 
 int tpo_chamfer_fwd(int dtype, int flags, const void* xyz1, const void* xyz2, int64_t B,
@@ -122,7 +123,8 @@ int tpo_chamfer_fwd(int dtype, int flags, const void* xyz1, const void* xyz2, in
     if ((s = cuda_status(cudaMemsetAsync(workspace, 0xff, need, st)))) return s;
     if ((s = chamfer_fwd_keys(dtype, flags, xyz1, xyz2, B, N, M, 0, N, k1, k2, st))) return s;
   }
-  return chamfer_finalize(dtype, flags, xyz1, xyz2, B, N, M, 0, N, k1, k2, dist1, idx1, dist2, idx2, st);
+  return chamfer_finalize(dtype, flags, xyz1, xyz2, B, N, M, 0, N, k1, k2, dist1, idx1, dist2, idx2,
+                          true, nullptr, 0, nullptr, st);
 }
 
 int tpo_chamfer_bwd(int dtype, const void* xyz1, const void* xyz2, int64_t B, int64_t N,
@@ -139,7 +141,7 @@ int tpo_chamfer_bwd(int dtype, const void* xyz1, const void* xyz2, int64_t B, in
   if (B * N > 0 && (s = cuda_status(cudaMemsetAsync(grad_xyz1, 0, es * 3 * B * N, st)))) return s;
   if (B * M > 0 && (s = cuda_status(cudaMemsetAsync(grad_xyz2, 0, es * 3 * B * M, st)))) return s;
   return chamfer_bwd_accumulate(dtype, xyz1, xyz2, B, N, M, 0, N, 0, M, idx1, idx2, grad_dist1,
-                                grad_dist2, grad_xyz1, grad_xyz2, st);
+                                grad_dist2, nullptr, 0, grad_xyz1, grad_xyz2, st);
 }
 
 int tpo_chamfer_bwd_partial(int dtype, const void* xyz1, const void* xyz2, int64_t B, int64_t N,
@@ -155,8 +157,58 @@ int tpo_chamfer_bwd_partial(int dtype, const void* xyz1, const void* xyz2, int64
   if ((B * N > 0 && !grad_xyz1) || (B * M > 0 && !grad_xyz2))
     return fail(TPO_ERR_INVALID_ARGUMENT, "chamfer_bwd_partial: null gradient output");
   return chamfer_bwd_accumulate(dtype, xyz1, xyz2, B, N, M, row_begin, row_end, col_begin, col_end,
-                                idx1, idx2, grad_dist1, grad_dist2, grad_xyz1, grad_xyz2,
-                                (cudaStream_t)stream);
+                                idx1, idx2, grad_dist1, grad_dist2, nullptr, 0, grad_xyz1,
+                                grad_xyz2, (cudaStream_t)stream);
+}
+
+size_t tpo_chamfer_loss_workspace_size(int dtype, int64_t B, int64_t N, int64_t M) {
+  if (!valid_dtype(dtype) || B < 0 || N < 0 || M < 0) return 0;
+  return tpo_chamfer_fwd_workspace_size(dtype, B, N, M) + align256(kFinLossWorkspace);
+}
+
+int tpo_chamfer_loss_fwd(int dtype, int flags, const void* xyz1, const void* xyz2, int64_t B,
+                         int64_t N, int64_t M, int reduction, void* loss, int32_t* idx1,
+                         int32_t* idx2, void* workspace, size_t workspace_bytes, void* stream) {
+  int s = check_chamfer_shape(dtype, xyz1, xyz2, B, N, M);
+  if (s) return s;
+  if (reduction != TPO_REDUCE_MEAN && reduction != TPO_REDUCE_SUM)
+    return fail(TPO_ERR_INVALID_ARGUMENT, "chamfer_loss: reduction must be TPO_REDUCE_MEAN or TPO_REDUCE_SUM");
+  if (!loss || (B * N > 0 && !idx1) || (B * M > 0 && !idx2))
+    return fail(TPO_ERR_INVALID_ARGUMENT, "chamfer_loss: null output");
+  const size_t need = tpo_chamfer_loss_workspace_size(dtype, B, N, M);
+  if (!workspace || workspace_bytes < need || (uintptr_t)workspace % 256)
+    return fail(TPO_ERR_WORKSPACE, "chamfer_loss: workspace missing, unaligned or smaller than tpo_chamfer_loss_workspace_size()");
+  cudaStream_t st = (cudaStream_t)stream;
+  const size_t kb = (size_t)tpo_chamfer_key_bytes(dtype);
+  const size_t keys_bytes = tpo_chamfer_fwd_workspace_size(dtype, B, N, M);
+  char* k1 = (char*)workspace;
+  char* k2 = k1 + align256(kb * (size_t)B * (size_t)N);
+  char* lw = k1 + keys_bytes;
+  if (keys_bytes && (s = cuda_status(cudaMemsetAsync(workspace, 0xff, keys_bytes, st)))) return s;
+  if ((s = cuda_status(cudaMemsetAsync(lw + kFinPartialBytes, 0, 256, st)))) return s;
+  if (B > 0 && N > 0 && M > 0 &&
+      (s = chamfer_fwd_keys(dtype, flags, xyz1, xyz2, B, N, M, 0, N, k1, k2, st)))
+    return s;
+  return chamfer_finalize(dtype, flags, xyz1, xyz2, B, N, M, 0, N, k1, k2, nullptr, idx1, nullptr,
+                          idx2, true, loss, reduction, lw, st);
+}
+
+int tpo_chamfer_loss_bwd(int dtype, const void* xyz1, const void* xyz2, int64_t B, int64_t N,
+                         int64_t M, int reduction, const int32_t* idx1, const int32_t* idx2,
+                         const void* grad_loss, void* grad_xyz1, void* grad_xyz2, void* stream) {
+  int s = check_chamfer_shape(dtype, xyz1, xyz2, B, N, M);
+  if (s) return s;
+  if (reduction != TPO_REDUCE_MEAN && reduction != TPO_REDUCE_SUM)
+    return fail(TPO_ERR_INVALID_ARGUMENT, "chamfer_loss_bwd: bad reduction");
+  if (!grad_loss || (B * N > 0 && (!grad_xyz1 || !idx1)) || (B * M > 0 && (!grad_xyz2 || !idx2)))
+    return fail(TPO_ERR_INVALID_ARGUMENT, "chamfer_loss_bwd: null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  const size_t es = (size_t)dtype_size(dtype);
+  if (B * N > 0 && (s = cuda_status(cudaMemsetAsync(grad_xyz1, 0, es * 3 * B * N, st)))) return s;
+  if (B * M > 0 && (s = cuda_status(cudaMemsetAsync(grad_xyz2, 0, es * 3 * B * M, st)))) return s;
+  return chamfer_bwd_accumulate(dtype, xyz1, xyz2, B, N, M, 0, N, 0, M, idx1, idx2, nullptr,
+                                nullptr, grad_loss, reduction == TPO_REDUCE_MEAN ? 1 : 2,
+                                grad_xyz1, grad_xyz2, st);
 }
 
 static int check_knn(int dtype, const void* p1, const void* p2, int64_t N, int64_t P1, int64_t P2,

@@ -20,6 +20,7 @@ struct BwdOps<float> {
   __device__ static float term(float g2, float a, float b) { return __fmul_rn(g2, __fsub_rn(a, b)); }
   __device__ static void add(float* p, float v) { atomicAdd(p, v); }
   __device__ static float neg(float v) { return -v; }
+  __device__ static float div(float g, int64_t n) { return __fdiv_rn(g, (float)n); }
 };
 template <>
 struct BwdOps<double> {
@@ -27,6 +28,7 @@ struct BwdOps<double> {
   __device__ static double term(double g2, double a, double b) { return __dmul_rn(g2, __dsub_rn(a, b)); }
   __device__ static void add(double* p, double v) { atomicAdd(p, v); }
   __device__ static double neg(double v) { return -v; }
+  __device__ static double div(double g, int64_t n) { return __ddiv_rn(g, (double)n); }
 };
 template <>
 struct BwdOps<__half> {
@@ -34,6 +36,7 @@ struct BwdOps<__half> {
   __device__ static __half term(__half g2, __half a, __half b) { return hmul_rn(g2, hsub_rn(a, b)); }
   __device__ static void add(__half* p, __half v) { atomicAdd(p, v); }
   __device__ static __half neg(__half v) { return __hneg(v); }
+  __device__ static __half div(__half g, int64_t n) { return __float2half_rn(__half2float(g) / (float)n); }
 };
 
 template <typename T>
@@ -41,11 +44,19 @@ __global__ void chamfer_bwd_kernel(const T* __restrict__ x1, const T* __restrict
                                    int64_t N, int64_t M, int64_t r0, int64_t r1, int64_t c0,
                                    int64_t c1, const int32_t* __restrict__ i1,
                                    const int32_t* __restrict__ i2, const T* __restrict__ g1,
-                                   const T* __restrict__ g2, T* __restrict__ gx1,
-                                   T* __restrict__ gx2) {
+                                   const T* __restrict__ g2, const T* __restrict__ gs,
+                                   int scalar_mode, T* __restrict__ gx1, T* __restrict__ gx2) {
   using O = BwdOps<T>;
-  const int64_t nr = (g1 && M > 0) ? r1 - r0 : 0;
-  const int64_t nc = (g2 && N > 0) ? c1 - c0 : 0;
+  // scalar_mode: 0 per-point grads g1/g2; 1 loss = mean(d1)+mean(d2) (grad gs/(B*N),
+  // gs/(B*M), as torch's MeanBackward divides); 2 loss = sum(d1)+sum(d2) (grad gs)
+  T gs1 = T(0.0f), gs2 = T(0.0f);
+  if (scalar_mode) {
+    const T g = *gs;
+    gs1 = scalar_mode == 1 ? O::div(g, B * N) : g;
+    gs2 = scalar_mode == 1 ? O::div(g, B * M) : g;
+  }
+  const int64_t nr = ((g1 || scalar_mode) && M > 0) ? r1 - r0 : 0;
+  const int64_t nc = ((g2 || scalar_mode) && N > 0) ? c1 - c0 : 0;
   const int64_t n1 = B * nr;
   const int64_t total = n1 + B * nc;
   for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total;
@@ -61,7 +72,7 @@ __global__ void chamfer_bwd_kernel(const T* __restrict__ x1, const T* __restrict
       pb = x2 + (b * M + j) * 3;
       ga = gx1 + o * 3;
       gb = gx2 + (b * M + j) * 3;
-      g = g1[o];
+      g = scalar_mode ? gs1 : g1[o];
     } else {
       const int64_t u = t - n1;
       const int64_t b = u / nc, j = c0 + u % nc;
@@ -71,7 +82,7 @@ __global__ void chamfer_bwd_kernel(const T* __restrict__ x1, const T* __restrict
       pb = x1 + (b * N + i) * 3;
       ga = gx2 + o * 3;
       gb = gx1 + (b * N + i) * 3;
-      g = g2[o];
+      g = scalar_mode ? gs2 : g2[o];
     }
     const T gg = O::two_g(g);
 #pragma unroll
@@ -86,31 +97,32 @@ __global__ void chamfer_bwd_kernel(const T* __restrict__ x1, const T* __restrict
 template <typename T>
 static int launch_bwd(const T* x1, const T* x2, int64_t B, int64_t N, int64_t M, int64_t r0,
                       int64_t r1, int64_t c0, int64_t c1, const int32_t* i1, const int32_t* i2,
-                      const T* g1, const T* g2, T* gx1, T* gx2, cudaStream_t st) {
-  const int64_t total = B * ((g1 && M > 0) ? r1 - r0 : 0) + B * ((g2 && N > 0) ? c1 - c0 : 0);
+                      const T* g1, const T* g2, const T* gs, int sm, T* gx1, T* gx2,
+                      cudaStream_t st) {
+  const int64_t total = B * (((g1 || sm) && M > 0) ? r1 - r0 : 0) + B * (((g2 || sm) && N > 0) ? c1 - c0 : 0);
   if (total <= 0) return TPO_OK;
   const int threads = 256;
   const int64_t blocks = std::min<int64_t>((total + threads - 1) / threads, 148 * 16);
   chamfer_bwd_kernel<T><<<(unsigned)blocks, threads, 0, st>>>(x1, x2, B, N, M, r0, r1, c0, c1, i1,
-                                                               i2, g1, g2, gx1, gx2);
+                                                               i2, g1, g2, gs, sm, gx1, gx2);
   return check_launch();
 }
 
 int chamfer_bwd_accumulate(int dtype, const void* x1, const void* x2, int64_t B, int64_t N,
                            int64_t M, int64_t r0, int64_t r1, int64_t c0, int64_t c1,
                            const int32_t* i1, const int32_t* i2, const void* g1, const void* g2,
-                           void* gx1, void* gx2, cudaStream_t st) {
+                           const void* gs, int sm, void* gx1, void* gx2, cudaStream_t st) {
   switch (dtype) {
     case TPO_F32:
       return launch_bwd<float>((const float*)x1, (const float*)x2, B, N, M, r0, r1, c0, c1, i1, i2,
-                               (const float*)g1, (const float*)g2, (float*)gx1, (float*)gx2, st);
+                               (const float*)g1, (const float*)g2, (const float*)gs, sm, (float*)gx1, (float*)gx2, st);
     case TPO_F16:
       return launch_bwd<__half>((const __half*)x1, (const __half*)x2, B, N, M, r0, r1, c0, c1, i1,
-                                i2, (const __half*)g1, (const __half*)g2, (__half*)gx1,
+                                i2, (const __half*)g1, (const __half*)g2, (const __half*)gs, sm, (__half*)gx1,
                                 (__half*)gx2, st);
     case TPO_F64:
       return launch_bwd<double>((const double*)x1, (const double*)x2, B, N, M, r0, r1, c0, c1, i1,
-                                i2, (const double*)g1, (const double*)g2, (double*)gx1,
+                                i2, (const double*)g1, (const double*)g2, (const double*)gs, sm, (double*)gx1,
                                 (double*)gx2, st);
   }
   return TPO_ERR_INVALID_ARGUMENT;

@@ -32,22 +32,46 @@
 namespace tpo {
 
 // ----------------------------- fp32 fast path -----------------------------
-constexpr int CF_R = 16;              // rows per lane
+#ifndef TPO_CF_R
+#define TPO_CF_R 16
+#endif
+#ifndef TPO_CF_MINB
+#define TPO_CF_MINB 1
+#endif
+constexpr int CF_R = TPO_CF_R;        // rows per lane
 constexpr int CF_RP = CF_R / 2;       // packed row pairs per lane
-constexpr int CF_C = 4;               // columns per step (= row-side chunk)
+constexpr int CF_C = 4;               // columns per sub-step
+constexpr int CF_CHUNK = 2 * CF_C;    // row-side chunk (columns per key)
 constexpr int CF_TILE_STEPS = 64;     // steps per shared-memory tile
 constexpr int CF_TILE = CF_TILE_STEPS * CF_C;
 constexpr int CF_MAXW = 4;            // warps per CTA
 constexpr int CF_ROWS_PER_WARP = 32 * CF_R;
 
+// min over R values with 3-input FMNMX, as a balanced tree
+template <int R>
+__device__ __forceinline__ float col_min(const float* v) {
+  if constexpr (R == 16) {
+    const float m5 = min3f(min3f(v[0], v[1], v[2]), min3f(v[3], v[4], v[5]), min3f(v[6], v[7], v[8]));
+    const float m6 = min3f(min3f(v[9], v[10], v[11]), min3f(v[12], v[13], v[14]), v[15]);
+    return fminf(m5, m6);
+  } else if constexpr (R == 8) {
+    return min3f(min3f(v[0], v[1], v[2]), min3f(v[3], v[4], v[5]), fminf(v[6], v[7]));
+  } else {
+    float m = v[0];
+#pragma unroll
+    for (int i = 1; i < R; ++i) m = fminf(m, v[i]);
+    return m;
+  }
+}
+
 template <int MODE>
-__global__ void __launch_bounds__(CF_MAXW * 32)
+__global__ void __launch_bounds__(CF_MAXW * 32, TPO_CF_MINB)
     chamfer_keys_f32_kernel(const float* __restrict__ xyz1, const float* __restrict__ xyz2,
                             int64_t N, int64_t M, int64_t row_begin, int64_t row_end,
                             int rb_count, int cs_count, int64_t seg,
                             u64* __restrict__ keys1, u64* __restrict__ keys2) {
   __shared__ __align__(16) float2 s_col[CF_TILE_STEPS][3][CF_C];
-  __shared__ __align__(16) u64 s_key[CF_MAXW][CF_TILE];
+  __shared__ __align__(16) uint2 s_wb[CF_MAXW][CF_TILE];  // {ballot, distance bits}
 
   const int W = blockDim.x >> 5;
   const int warp = threadIdx.x >> 5;
@@ -93,7 +117,7 @@ __global__ void __launch_bounds__(CF_MAXW * 32)
 
   for (int64_t tc = c0; tc < c1; tc += CF_TILE) {
     const int ncols = (int)min64(CF_TILE, c1 - tc);
-    const int nsteps = (ncols + CF_C - 1) / CF_C;
+    const int nsteps = ((ncols + CF_CHUNK - 1) / CF_CHUNK) * 2;  // even: 8-column chunks
     __syncthreads();
     {
       const float* src = xyz2 + (b * M + tc) * 3;
@@ -108,53 +132,62 @@ __global__ void __launch_bounds__(CF_MAXW * 32)
     }
     __syncthreads();
     if (warp_active) {
+      // Two 4-column sub-steps per iteration; the row-side chunk is 8 columns.
 #pragma unroll 1
-      for (int s = 0; s < nsteps; ++s) {
-        const ulonglong2* cp = reinterpret_cast<const ulonglong2*>(&s_col[s][0][0]);
-        const ulonglong2 xa = cp[0], xb = cp[1], ya = cp[2], yb = cp[3], za = cp[4], zb = cp[5];
-        const u64 X[CF_C] = {xa.x, xa.y, xb.x, xb.y};
-        const u64 Y[CF_C] = {ya.x, ya.y, yb.x, yb.y};
-        const u64 Z[CF_C] = {za.x, za.y, zb.x, zb.y};
-        float d[CF_C][CF_R];
+      for (int s = 0; s < nsteps; s += 2) {
+        float rm[CF_R];
 #pragma unroll
-        for (int c = 0; c < CF_C; ++c) {
+        for (int h = 0; h < 2; ++h) {
+          const ulonglong2* cp = reinterpret_cast<const ulonglong2*>(&s_col[s + h][0][0]);
+          const ulonglong2 xa = cp[0], xb = cp[1], ya = cp[2], yb = cp[3], za = cp[4], zb = cp[5];
+          const u64 X[CF_C] = {xa.x, xa.y, xb.x, xb.y};
+          const u64 Y[CF_C] = {ya.x, ya.y, yb.x, yb.y};
+          const u64 Z[CF_C] = {za.x, za.y, zb.x, zb.y};
+          float d[CF_C][CF_R];
 #pragma unroll
-          for (int p = 0; p < CF_RP; ++p) {
-            const u64 t = dist2x2<MODE>(sub2(X[c], QX[p]), sub2(Y[c], QY[p]), sub2(Z[c], QZ[p]));
-            upk(t, d[c][2 * p], d[c][2 * p + 1]);
+          for (int c = 0; c < CF_C; ++c) {
+#pragma unroll
+            for (int p = 0; p < CF_RP; ++p) {
+              const u64 t = dist2x2<MODE>(sub2(X[c], QX[p]), sub2(Y[c], QY[p]), sub2(Z[c], QZ[p]));
+              upk(t, d[c][2 * p], d[c][2 * p + 1]);
+            }
+          }
+#pragma unroll
+          for (int r = 0; r < CF_R; ++r) {
+            const float m = min3f(h == 0 ? best[r] : rm[r], d[0][r], d[1][r]);
+            rm[r] = min3f(m, d[2][r], d[3][r]);
+          }
+          // column side: warp min of the lanes' partial minima (bit pattern of a
+          // non-negative float orders like its value; NaN padding sorts last) and
+          // the ballot of lanes holding it -- the winning lane is resolved later
+#pragma unroll
+          for (int c = 0; c < CF_C; ++c) {
+            const unsigned u = __float_as_uint(col_min<CF_R>(d[c]));
+            const unsigned w = redux_min_u32(u);
+            const unsigned bal = __ballot_sync(0xffffffffu, u == w);
+            if (lane == 0) s_wb[warp][(s + h) * CF_C + c] = make_uint2(bal, w);
           }
         }
         const int colbase = (int)(tc + s * CF_C);
 #pragma unroll
         for (int r = 0; r < CF_R; ++r) {
-          float nb = min3f(best[r], d[0][r], d[1][r]);
-          nb = min3f(nb, d[2][r], d[3][r]);
-          if (nb < best[r]) bchunk[r] = colbase;
-          best[r] = nb;
-        }
-#pragma unroll
-        for (int c = 0; c < CF_C; ++c) {
-          const float m0 = min3f(d[c][0], d[c][1], d[c][2]);
-          const float m1 = min3f(d[c][3], d[c][4], d[c][5]);
-          const float m2 = min3f(d[c][6], d[c][7], d[c][8]);
-          const float m3 = min3f(d[c][9], d[c][10], d[c][11]);
-          const float m4 = min3f(d[c][12], d[c][13], d[c][14]);
-          const float m5 = min3f(m0, m1, m2);
-          const float m6 = min3f(m3, m4, d[c][15]);
-          const unsigned u = __float_as_uint(fminf(m5, m6));
-          const unsigned w = redux_min_u32(u);
-          const unsigned bal = __ballot_sync(0xffffffffu, u == w);
-          const int win = __ffs(bal) - 1;
-          if (lane == 0)
-            s_key[warp][s * CF_C + c] =
-                ((u64)w << 32) | (unsigned)(warp_row0 + (int64_t)win * CF_R);
+          if (rm[r] < best[r]) bchunk[r] = colbase;
+          best[r] = rm[r];
         }
       }
     }
     __syncthreads();
+    // merge the warps' column results (lowest row chunk on equal distance) and
+    // fold them into the global keys
     for (int col = threadIdx.x; col < ncols; col += blockDim.x) {
-      u64 k = s_key[0][col];
-      for (int w = 1; w < n_active; ++w) k = min(k, s_key[w][col]);
+      u64 k = ~0ull;
+      for (int w = 0; w < n_active; ++w) {
+        const uint2 e = s_wb[w][col];
+        const unsigned win = __ffs(e.x) - 1;
+        const u64 kw = ((u64)e.y << 32) |
+                       (unsigned)(blk_row0 + (int64_t)w * CF_ROWS_PER_WARP + (int64_t)win * CF_R);
+        k = min(k, kw);
+      }
       red_min_u64(keys2 + b * M + tc + col, k);
     }
   }
@@ -393,8 +426,37 @@ struct FinTraits<double> {
   __device__ static double value(K k) { return __longlong_as_double((long long)k.hi); }
 };
 
-// One thread per output point.  Rows: key chunk = first of `row_chunk` columns
-// (4).  Columns: key chunk = first of `col_chunk` rows (R of the keys kernel).
+template <typename T>
+struct FinRound {
+  __device__ static T from(double v) { return (T)v; }
+  __device__ static T add(T a, T b) { return a + b; }
+};
+template <>
+struct FinRound<__half> {
+  __device__ static __half from(double v) { return __float2half_rn((float)v); }
+  __device__ static __half add(__half a, __half b) { return hadd_rn(a, b); }
+};
+
+// Optional fused reduction of the forward (ChamferDistance "mean"/"sum"): each
+// block sums its points' distances in a fixed order, writes a partial, and the
+// last block to finish adds the partials in block order -- deterministic for a
+// given grid.  partials/counter live in the caller's workspace; counter starts 0.
+template <typename T>
+struct FinLoss {
+  double* partials;   // 2 per block: sum(dist1), sum(dist2)
+  unsigned* counter;  // blocks done
+  T* loss;            // nullptr: no reduction
+  int reduction;      // 0 mean(d1)+mean(d2), 1 sum(d1)+sum(d2)
+};
+
+template <typename T>
+__device__ __forceinline__ double to_d(T v) { return (double)v; }
+template <>
+__device__ __forceinline__ double to_d<__half>(__half v) { return (double)__half2float(v); }
+
+// One thread per output point.  Rows: key chunk = first of `row_chunk` columns.
+// Columns: key chunk = first of `col_chunk` rows (R of the keys kernel).
+// dist1 / dist2 may be null (loss-only use); do_cols selects the column side.
 template <typename T, int MODE>
 __global__ void chamfer_finalize_kernel(const T* __restrict__ xyz1, const T* __restrict__ xyz2,
                                         int64_t B, int64_t N, int64_t M, int64_t row_begin,
@@ -402,11 +464,13 @@ __global__ void chamfer_finalize_kernel(const T* __restrict__ xyz1, const T* __r
                                         const typename FinTraits<T>::K* __restrict__ keys1,
                                         const typename FinTraits<T>::K* __restrict__ keys2,
                                         T* __restrict__ dist1, int32_t* __restrict__ idx1,
-                                        T* __restrict__ dist2, int32_t* __restrict__ idx2) {
+                                        T* __restrict__ dist2, int32_t* __restrict__ idx2,
+                                        bool do_cols, FinLoss<T> fl) {
   using F = FinTraits<T>;
   const int64_t nrows = row_end - row_begin;
   const int64_t n1 = B * nrows;
-  const int64_t total = n1 + (dist2 ? B * M : 0);
+  const int64_t total = n1 + (do_cols ? B * M : 0);
+  double s1 = 0.0, s2 = 0.0;
   for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total;
        t += (int64_t)gridDim.x * blockDim.x) {
     if (t < n1) {
@@ -424,8 +488,9 @@ __global__ void chamfer_finalize_kernel(const T* __restrict__ xyz1, const T* __r
           if (F::template same<MODE>(a, xyz2 + (b * M + j) * 3, key)) { ix = (int32_t)j; break; }
         dv = F::value(key);
       }
-      dist1[o] = dv;
+      if (dist1) dist1[o] = dv;
       idx1[o] = ix;
+      s1 += to_d(dv);
     } else {
       const int64_t u = t - n1;
       const int64_t b = u / M, j = u % M;
@@ -442,10 +507,49 @@ __global__ void chamfer_finalize_kernel(const T* __restrict__ xyz1, const T* __r
           if (F::template same<MODE>(xyz1 + (b * N + i) * 3, c, key)) { ix = (int32_t)i; break; }
         dv = F::value(key);
       }
-      dist2[o] = dv;
+      if (dist2) dist2[o] = dv;
       idx2[o] = ix;
+      s2 += to_d(dv);
     }
   }
+  if (fl.loss == nullptr) return;
+  // block reduction (fixed order), then the last block folds the partials
+  __shared__ double r1[32], r2[32];
+#pragma unroll
+  for (int off = 16; off; off >>= 1) {
+    s1 += __shfl_down_sync(0xffffffffu, s1, off);
+    s2 += __shfl_down_sync(0xffffffffu, s2, off);
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  if (lane == 0) { r1[warp] = s1; r2[warp] = s2; }
+  __syncthreads();
+  __shared__ bool last;
+  if (threadIdx.x == 0) {
+    double a = 0.0, c = 0.0;
+    for (int w = 0; w < nw; ++w) { a += r1[w]; c += r2[w]; }
+    fl.partials[2 * blockIdx.x] = a;
+    fl.partials[2 * blockIdx.x + 1] = c;
+    __threadfence();
+    last = atomicAdd(fl.counter, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!last || threadIdx.x != 0) return;
+  __threadfence();
+  double a = 0.0, c = 0.0;
+  for (unsigned k = 0; k < gridDim.x; ++k) {
+    a += __ldcg(fl.partials + 2 * k);
+    c += __ldcg(fl.partials + 2 * k + 1);
+  }
+  // torch semantics: mean(d1) + mean(d2) (or sums), each term rounded to T, added in T
+  T t1, t2;
+  if (fl.reduction == 0) {
+    t1 = FinRound<T>::from(B * N > 0 ? a / (double)(B * N) : __longlong_as_double(0x7ff8000000000000ll));
+    t2 = FinRound<T>::from(B * M > 0 ? c / (double)(B * M) : __longlong_as_double(0x7ff8000000000000ll));
+  } else {
+    t1 = FinRound<T>::from(a);
+    t2 = FinRound<T>::from(c);
+  }
+  *fl.loss = FinRound<T>::add(t1, t2);
 }
 
 // ------------------------------- host side -------------------------------
@@ -533,15 +637,22 @@ int launch_keys_generic(const T* x1, const T* x2, int64_t B, int64_t N, int64_t 
 
 template <typename T, int MODE>
 int launch_finalize(const T* x1, const T* x2, int64_t B, int64_t N, int64_t M, int64_t rb0,
-                    int64_t rb1, int col_chunk, const void* k1, const void* k2, T* d1, int32_t* i1,
-                    T* d2, int32_t* i2, cudaStream_t st) {
-  const int64_t total = B * (rb1 - rb0) + (d2 ? B * M : 0);
-  if (total <= 0) return TPO_OK;
+                    int64_t rb1, int row_chunk, int col_chunk, const void* k1, const void* k2,
+                    T* d1, int32_t* i1, T* d2, int32_t* i2, bool do_cols, T* loss,
+                    int reduction, void* loss_ws, cudaStream_t st) {
+  const int64_t total = B * (rb1 - rb0) + (do_cols ? B * M : 0);
+  if (total <= 0 && loss == nullptr) return TPO_OK;
   const int threads = 256;
-  const int64_t blocks = std::min<int64_t>((total + threads - 1) / threads, 148 * 32);
+  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((total + threads - 1) / threads,
+                                                                 kFinMaxBlocks));
+  FinLoss<T> fl;
+  fl.loss = loss;
+  fl.reduction = reduction;
+  fl.partials = (double*)loss_ws;
+  fl.counter = loss_ws ? (unsigned*)((char*)loss_ws + kFinPartialBytes) : nullptr;
   chamfer_finalize_kernel<T, MODE><<<(unsigned)blocks, threads, 0, st>>>(
-      x1, x2, B, N, M, rb0, rb1, CF_C, col_chunk, (const typename FinTraits<T>::K*)k1,
-      (const typename FinTraits<T>::K*)k2, d1, i1, d2, i2);
+      x1, x2, B, N, M, rb0, rb1, row_chunk, col_chunk, (const typename FinTraits<T>::K*)k1,
+      (const typename FinTraits<T>::K*)k2, d1, i1, d2, i2, do_cols, fl);
   return check_launch();
 }
 
@@ -566,18 +677,21 @@ int chamfer_fwd_keys(int dtype, int flags, const void* x1, const void* x2, int64
 
 int chamfer_finalize(int dtype, int flags, const void* x1, const void* x2, int64_t B, int64_t N,
                      int64_t M, int64_t rb0, int64_t rb1, const void* k1, const void* k2, void* d1,
-                     int32_t* i1, void* d2, int32_t* i2, cudaStream_t st) {
+                     int32_t* i1, void* d2, int32_t* i2, bool do_cols, void* loss, int reduction,
+                     void* loss_ws, cudaStream_t st) {
   const bool exact = (flags & TPO_ROUND_EXACT) != 0;
+#define TPO_FIN(T, MODE, CH, CC)                                                                 \
+  launch_finalize<T, MODE>((const T*)x1, (const T*)x2, B, N, M, rb0, rb1, CH, CC, k1, k2, (T*)d1, \
+                           i1, (T*)d2, i2, do_cols, (T*)loss, reduction, loss_ws, st)
   switch (dtype) {
     case TPO_F32:
-      return exact ? launch_finalize<float, TPO_ROUND_EXACT>((const float*)x1, (const float*)x2, B, N, M, rb0, rb1, CF_R, k1, k2, (float*)d1, i1, (float*)d2, i2, st)
-                   : launch_finalize<float, TPO_ROUND_FMA>((const float*)x1, (const float*)x2, B, N, M, rb0, rb1, CF_R, k1, k2, (float*)d1, i1, (float*)d2, i2, st);
+      return exact ? TPO_FIN(float, TPO_ROUND_EXACT, CF_CHUNK, CF_R) : TPO_FIN(float, TPO_ROUND_FMA, CF_CHUNK, CF_R);
     case TPO_F16:
-      return launch_finalize<__half, TPO_ROUND_EXACT>((const __half*)x1, (const __half*)x2, B, N, M, rb0, rb1, CG_R, k1, k2, (__half*)d1, i1, (__half*)d2, i2, st);
+      return TPO_FIN(__half, TPO_ROUND_EXACT, CG_C, CG_R);
     case TPO_F64:
-      return exact ? launch_finalize<double, TPO_ROUND_EXACT>((const double*)x1, (const double*)x2, B, N, M, rb0, rb1, CG_R, k1, k2, (double*)d1, i1, (double*)d2, i2, st)
-                   : launch_finalize<double, TPO_ROUND_FMA>((const double*)x1, (const double*)x2, B, N, M, rb0, rb1, CG_R, k1, k2, (double*)d1, i1, (double*)d2, i2, st);
+      return exact ? TPO_FIN(double, TPO_ROUND_EXACT, CG_C, CG_R) : TPO_FIN(double, TPO_ROUND_FMA, CG_C, CG_R);
   }
+#undef TPO_FIN
   return TPO_ERR_INVALID_ARGUMENT;
 }
 

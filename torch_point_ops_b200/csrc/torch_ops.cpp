@@ -93,6 +93,50 @@ std::tuple<at::Tensor, at::Tensor> chamfer_backward(const at::Tensor& xyz1_, con
   return {gx1, gx2};
 }
 
+// ---- fused ChamferDistance loss (reduction 0 = mean, 1 = sum) ----
+std::tuple<at::Tensor, at::Tensor, at::Tensor> chamfer_loss(const at::Tensor& xyz1_,
+                                                            const at::Tensor& xyz2_,
+                                                            int64_t reduction, int64_t flags) {
+  check_cloud(xyz1_, "xyz1");
+  check_cloud(xyz2_, "xyz2");
+  TORCH_CHECK(xyz1_.size(2) == 3 && xyz2_.size(2) == 3, "chamfer: points must be 3-D");
+  TORCH_CHECK(xyz1_.size(0) == xyz2_.size(0), "chamfer: batch sizes differ");
+  TORCH_CHECK(xyz1_.scalar_type() == xyz2_.scalar_type(), "chamfer: dtypes differ");
+  const c10::cuda::CUDAGuard g(xyz1_.device());
+  const at::Tensor xyz1 = xyz1_.contiguous(), xyz2 = xyz2_.contiguous();
+  const int64_t B = xyz1.size(0), N = xyz1.size(1), M = xyz2.size(1);
+  const int dt = to_dtype(xyz1);
+  auto loss = at::empty({}, xyz1.options());
+  auto idx1 = at::empty({B, N}, xyz1.options().dtype(at::kInt));
+  auto idx2 = at::empty({B, M}, xyz1.options().dtype(at::kInt));
+  const size_t ws_bytes = tpo_chamfer_loss_workspace_size(dt, B, N, M);
+  auto ws = at::empty({(int64_t)ws_bytes}, xyz1.options().dtype(at::kByte));
+  ok(tpo_chamfer_loss_fwd(dt, (int)flags, xyz1.data_ptr(), xyz2.data_ptr(), B, N, M, (int)reduction,
+                          loss.data_ptr(), idx1.data_ptr<int32_t>(), idx2.data_ptr<int32_t>(),
+                          ws.data_ptr(), ws_bytes, stream_of(xyz1)),
+     "chamfer_loss");
+  return {loss, idx1, idx2};
+}
+
+std::tuple<at::Tensor, at::Tensor> chamfer_loss_backward(const at::Tensor& xyz1_,
+                                                         const at::Tensor& xyz2_,
+                                                         const at::Tensor& idx1,
+                                                         const at::Tensor& idx2,
+                                                         const at::Tensor& grad_loss,
+                                                         int64_t reduction) {
+  const c10::cuda::CUDAGuard g(xyz1_.device());
+  const at::Tensor xyz1 = xyz1_.contiguous(), xyz2 = xyz2_.contiguous();
+  const int64_t B = xyz1.size(0), N = xyz1.size(1), M = xyz2.size(1);
+  const at::Tensor gl = grad_loss.to(xyz1.scalar_type()).reshape({1}).contiguous();
+  auto gx1 = at::empty_like(xyz1);
+  auto gx2 = at::empty_like(xyz2);
+  ok(tpo_chamfer_loss_bwd(to_dtype(xyz1), xyz1.data_ptr(), xyz2.data_ptr(), B, N, M, (int)reduction,
+                          idx1.data_ptr<int32_t>(), idx2.data_ptr<int32_t>(), gl.data_ptr(),
+                          gx1.data_ptr(), gx2.data_ptr(), stream_of(xyz1)),
+     "chamfer_loss_backward");
+  return {gx1, gx2};
+}
+
 // ---- row-sharded split (multi-GPU): keys live in int64 tensors ----
 at::Tensor chamfer_keys_empty(const at::Tensor& like, int64_t n) {
   const int dt = to_dtype(like);
@@ -254,6 +298,9 @@ TORCH_LIBRARY(torch_point_ops_b200_chamfer, m) {
   m.def("chamfer_backward(Tensor xyz1, Tensor xyz2, Tensor idx1, Tensor idx2, "
         "Tensor grad_dist1, Tensor grad_dist2) -> (Tensor, Tensor)");
   m.def("chamfer_forward_ex(Tensor xyz1, Tensor xyz2, int flags) -> (Tensor, Tensor, Tensor, Tensor)");
+  m.def("chamfer_loss(Tensor xyz1, Tensor xyz2, int reduction, int flags) -> (Tensor, Tensor, Tensor)");
+  m.def("chamfer_loss_backward(Tensor xyz1, Tensor xyz2, Tensor idx1, Tensor idx2, "
+        "Tensor grad_loss, int reduction) -> (Tensor, Tensor)");
   m.def("chamfer_keys_empty(Tensor like, int n) -> Tensor");
   m.def("chamfer_fwd_keys(Tensor xyz1, Tensor xyz2, int row_begin, int row_end, int flags, "
         "Tensor(a!) keys1, Tensor(b!) keys2) -> ()");
@@ -268,6 +315,8 @@ TORCH_LIBRARY_IMPL(torch_point_ops_b200_chamfer, CUDA, m) {
   m.impl("chamfer_forward", &chamfer_forward);
   m.impl("chamfer_backward", &chamfer_backward);
   m.impl("chamfer_forward_ex", &chamfer_forward_ex);
+  m.impl("chamfer_loss", &chamfer_loss);
+  m.impl("chamfer_loss_backward", &chamfer_loss_backward);
   m.impl("chamfer_keys_empty", &chamfer_keys_empty);
   m.impl("chamfer_fwd_keys", &chamfer_fwd_keys);
   m.impl("chamfer_finalize", &chamfer_finalize);

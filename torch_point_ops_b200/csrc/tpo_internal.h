@@ -15,13 +15,21 @@ int check_launch();
 
 int chamfer_fwd_keys(int dtype, int flags, const void* x1, const void* x2, int64_t B, int64_t N,
                      int64_t M, int64_t rb0, int64_t rb1, void* k1, void* k2, cudaStream_t st);
+// Finalize keys into (dist, idx).  do_cols: also the column side.  loss != null:
+// fused reduction (0 = mean(d1)+mean(d2), 1 = sums) using loss_ws
+// (kFinLossWorkspace bytes, the counter word at kFinPartialBytes zeroed).
+constexpr int kFinMaxBlocks = 148 * 32;
+constexpr size_t kFinPartialBytes = (size_t)kFinMaxBlocks * 2 * sizeof(double);
+constexpr size_t kFinLossWorkspace = kFinPartialBytes + 256;
 int chamfer_finalize(int dtype, int flags, const void* x1, const void* x2, int64_t B, int64_t N,
                      int64_t M, int64_t rb0, int64_t rb1, const void* k1, const void* k2, void* d1,
-                     int32_t* i1, void* d2, int32_t* i2, cudaStream_t st);
+                     int32_t* i1, void* d2, int32_t* i2, bool do_cols, void* loss, int reduction,
+                     void* loss_ws, cudaStream_t st);
 int chamfer_bwd_accumulate(int dtype, const void* x1, const void* x2, int64_t B, int64_t N,
                            int64_t M, int64_t r0, int64_t r1, int64_t c0, int64_t c1,
                            const int32_t* i1, const int32_t* i2, const void* g1, const void* g2,
-                           void* gx1, void* gx2, cudaStream_t st);
+                           const void* gscalar, int scalar_mode, void* gx1, void* gx2,
+                           cudaStream_t st);
 int knn_forward(int dtype, int flags, const void* p1, const void* p2, const int64_t* l1,
                 const int64_t* l2, int64_t N, int64_t P1, int64_t P2, int64_t D, int64_t norm,
                 int64_t K, void* dists, int64_t* idxs, cudaStream_t st);
