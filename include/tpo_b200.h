@@ -74,6 +74,23 @@ TPO_API int tpo_chamfer_fwd(int dtype, int flags, const void* xyz1, const void* 
                     int64_t N, int64_t M, void* dist1, void* dist2, int32_t* idx1,
                     int32_t* idx2, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Allocation-free chamfer forward.  No counterpart in the reference.
+ * For callers that cannot allocate device memory (no cudaMalloc, no allocator
+ * they may call: code inside an allocator or memory pool, services that forbid
+ * device allocation after start-up, hosts that only receive buffers).  Same
+ * arguments and results as tpo_chamfer_fwd minus the workspace: the keys live
+ * in a 16 MiB device array owned by the library, which every GPU that loads the
+ * library holds until process exit.  Limit: tpo_chamfer_fwd_workspace_size()
+ * <= 16 MiB, i.e. B*(N+M) <= 2,097,152 points for f32/f16 (1,048,576 for f64);
+ * larger problems return TPO_ERR_WORKSPACE.  The first call on a device looks
+ * up the array's device address (cudaGetSymbolAddress) -- make that first call
+ * before any stream capture.  Calls share the array: calls that overlap on the
+ * GPU (other streams or threads on the same device) race and must be
+ * serialised by the caller.  Allocates nothing. */
+TPO_API int tpo_chamfer_fwd_noalloc(int dtype, int flags, const void* xyz1, const void* xyz2,
+                                    int64_t B, int64_t N, int64_t M, void* dist1, void* dist2,
+                                    int32_t* idx1, int32_t* idx2, void* stream);
+
 /* Split form of tpo_chamfer_fwd for row-sharded multi-GPU runs (one rank owns rows
  * [row_begin,row_end) of xyz1 and all of xyz2).  Keys are packed (distance bits,
  * candidate-chunk) words; their minimum over ranks is the global answer, so an

@@ -23,6 +23,8 @@ static int fail(int code, const char* what) {
   return code;
 }
 
+int set_error(int code, const char* msg) { return fail(code, msg); }
+
 static size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 
 }  // namespace tpo

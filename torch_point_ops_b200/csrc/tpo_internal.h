@@ -12,6 +12,8 @@ namespace tpo {
 int cuda_status(cudaError_t e);
 // cudaGetLastError() after a launch.
 int check_launch();
+// Records `msg` for tpo_status_string and returns `code`.
+int set_error(int code, const char* msg);
 
 int chamfer_fwd_keys(int dtype, int flags, const void* x1, const void* x2, int64_t B, int64_t N,
                      int64_t M, int64_t rb0, int64_t rb1, void* k1, void* k2, cudaStream_t st);
