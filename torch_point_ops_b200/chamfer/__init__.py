@@ -9,6 +9,8 @@ _ops = _lib.chamfer_ops
 
 def _chamfer_backward(ctx, grad_dist1, grad_dist2, grad_idx1, grad_idx2):
     xyz1, xyz2, idx1, idx2 = ctx.saved_tensors
+    if grad_dist1 is None and grad_dist2 is None:
+        return None, None
     if grad_dist1 is None:
         grad_dist1 = torch.zeros(idx1.shape, dtype=xyz1.dtype, device=xyz1.device)
     if grad_dist2 is None:
@@ -21,6 +23,7 @@ def _setup(ctx, inputs, output):
     xyz1, xyz2 = inputs[0], inputs[1]
     _, _, idx1, idx2 = output
     ctx.save_for_backward(xyz1, xyz2, idx1, idx2)
+    ctx.set_materialize_grads(False)
 
 
 def _backward_ex(ctx, g1, g2, gi1, gi2):
@@ -56,10 +59,13 @@ def _loss_setup(ctx, inputs, output):
     _, idx1, idx2 = output
     ctx.save_for_backward(xyz1, xyz2, idx1, idx2)
     ctx.reduction = reduction
+    ctx.set_materialize_grads(False)  # no zero tensors for the int outputs' grads
 
 
 def _loss_backward(ctx, grad_loss, gi1, gi2):
     xyz1, xyz2, idx1, idx2 = ctx.saved_tensors
+    if grad_loss is None:
+        return None, None, None, None
     gx1, gx2 = _ops.chamfer_loss_backward(xyz1, xyz2, idx1, idx2, grad_loss, ctx.reduction)
     return gx1, gx2, None, None
 

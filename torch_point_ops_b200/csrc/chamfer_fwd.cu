@@ -533,13 +533,26 @@ __global__ void chamfer_finalize_kernel(const T* __restrict__ xyz1, const T* __r
     last = atomicAdd(fl.counter, 1u) == gridDim.x - 1;
   }
   __syncthreads();
-  if (!last || threadIdx.x != 0) return;
+  if (!last) return;
   __threadfence();
+  // the last block folds the partials: fixed per-thread strides, then a fixed tree
   double a = 0.0, c = 0.0;
-  for (unsigned k = 0; k < gridDim.x; ++k) {
+  for (unsigned k = threadIdx.x; k < gridDim.x; k += blockDim.x) {
     a += __ldcg(fl.partials + 2 * k);
     c += __ldcg(fl.partials + 2 * k + 1);
   }
+#pragma unroll
+  for (int off = 16; off; off >>= 1) {
+    a += __shfl_down_sync(0xffffffffu, a, off);
+    c += __shfl_down_sync(0xffffffffu, c, off);
+  }
+  __syncthreads();
+  if (lane == 0) { r1[warp] = a; r2[warp] = c; }
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  a = 0.0;
+  c = 0.0;
+  for (int w = 0; w < nw; ++w) { a += r1[w]; c += r2[w]; }
   // torch semantics: mean(d1) + mean(d2) (or sums), each term rounded to T, added in T
   T t1, t2;
   if (fl.reduction == 0) {

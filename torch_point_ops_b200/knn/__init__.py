@@ -9,6 +9,8 @@ _ops = _lib.knn_ops
 
 def _knn_backward(ctx, grad_idxs, grad_dists):
     p1, p2, lengths1, lengths2, idxs = ctx.saved_tensors
+    if grad_dists is None:
+        return None, None, None, None, None, None, None
     grad_p1, grad_p2 = _ops.knn_backward(p1, p2, lengths1, lengths2, idxs, ctx.norm, grad_dists)
     return grad_p1, grad_p2, None, None, None, None, None
 
@@ -18,6 +20,7 @@ def _knn_setup_context(ctx, inputs, output):
     idxs, _ = output
     ctx.save_for_backward(p1, p2, lengths1, lengths2, idxs)
     ctx.norm = norm
+    ctx.set_materialize_grads(False)
 
 
 def _knn_backward_ex(ctx, gi, gd):
