@@ -186,8 +186,8 @@ int tpo_chamfer_loss_fwd(int dtype, int flags, const void* xyz1, const void* xyz
   char* k1 = (char*)workspace;
   char* k2 = k1 + align256(kb * (size_t)B * (size_t)N);
   char* lw = k1 + keys_bytes;
-  if (keys_bytes && (s = cuda_status(cudaMemsetAsync(workspace, 0xff, keys_bytes, st)))) return s;
-  if ((s = cuda_status(cudaMemsetAsync(lw + kFinPartialBytes, 0, 256, st)))) return s;
+  // one fill: keys to the empty key, the finalize counter (after the partials) to 0xffffffff
+  if ((s = cuda_status(cudaMemsetAsync(workspace, 0xff, need, st)))) return s;
   if (B > 0 && N > 0 && M > 0 &&
       (s = chamfer_fwd_keys(dtype, flags, xyz1, xyz2, B, N, M, 0, N, k1, k2, st)))
     return s;

@@ -58,8 +58,10 @@ __device__ __forceinline__ float col_min(const float* v) {
     return min3f(min3f(v[0], v[1], v[2]), min3f(v[3], v[4], v[5]), fminf(v[6], v[7]));
   } else {
     float m = v[0];
+    int i = 1;
 #pragma unroll
-    for (int i = 1; i < R; ++i) m = fminf(m, v[i]);
+    for (; i + 1 < R; i += 2) m = min3f(m, v[i], v[i + 1]);
+    if (i < R) m = fminf(m, v[i]);
     return m;
   }
 }
@@ -440,11 +442,11 @@ struct FinRound<__half> {
 // Optional fused reduction of the forward (ChamferDistance "mean"/"sum"): each
 // block sums its points' distances in a fixed order, writes a partial, and the
 // last block to finish adds the partials in block order -- deterministic for a
-// given grid.  partials/counter live in the caller's workspace; counter starts 0.
+// given grid.  partials/counter live in the caller's workspace.
 template <typename T>
 struct FinLoss {
   double* partials;   // 2 per block: sum(dist1), sum(dist2)
-  unsigned* counter;  // blocks done
+  unsigned* counter;  // blocks done, starting from 0xffffffff
   T* loss;            // nullptr: no reduction
   int reduction;      // 0 mean(d1)+mean(d2), 1 sum(d1)+sum(d2)
 };
@@ -454,13 +456,36 @@ __device__ __forceinline__ double to_d(T v) { return (double)v; }
 template <>
 __device__ __forceinline__ double to_d<__half>(__half v) { return (double)__half2float(v); }
 
+// First index in [base, end) whose distance to q has the key's exact bits.  All
+// candidate loads are issued before any compare (independent, unrolled), so the
+// scan costs one memory round trip instead of one per candidate.
+template <typename T, int MODE, int CH, bool Q_IS_ROW>
+__device__ __forceinline__ int32_t find_in_chunk(const T* q, const T* cloud, int64_t base,
+                                                 int64_t end, typename FinTraits<T>::K key) {
+  T c[CH][3];
+#pragma unroll
+  for (int k = 0; k < CH; ++k) {
+    const bool ok = base + k < end;
+#pragma unroll
+    for (int d = 0; d < 3; ++d) c[k][d] = ok ? cloud[(base + k) * 3 + d] : q[d];
+  }
+  int found = -1;
+#pragma unroll
+  for (int k = CH - 1; k >= 0; --k) {
+    const bool hit = Q_IS_ROW ? FinTraits<T>::template same<MODE>(q, c[k], key)
+                              : FinTraits<T>::template same<MODE>(c[k], q, key);
+    if (base + k < end && hit) found = k;
+  }
+  return (int32_t)(base + (found < 0 ? 0 : found));
+}
+
 // One thread per output point.  Rows: key chunk = first of `row_chunk` columns.
 // Columns: key chunk = first of `col_chunk` rows (R of the keys kernel).
 // dist1 / dist2 may be null (loss-only use); do_cols selects the column side.
-template <typename T, int MODE>
+template <typename T, int MODE, int ROWCH, int COLCH>
 __global__ void chamfer_finalize_kernel(const T* __restrict__ xyz1, const T* __restrict__ xyz2,
                                         int64_t B, int64_t N, int64_t M, int64_t row_begin,
-                                        int64_t row_end, int row_chunk, int col_chunk,
+                                        int64_t row_end,
                                         const typename FinTraits<T>::K* __restrict__ keys1,
                                         const typename FinTraits<T>::K* __restrict__ keys2,
                                         T* __restrict__ dist1, int32_t* __restrict__ idx1,
@@ -482,10 +507,9 @@ __global__ void chamfer_finalize_kernel(const T* __restrict__ xyz1, const T* __r
       if (M > 0 && !F::empty(key)) {
         const unsigned base = F::chunk(key);
         const T* a = xyz1 + o * 3;
-        ix = (int32_t)base;
-        const int64_t end = min64(M, (int64_t)base + row_chunk);
-        for (int64_t j = base; j < end; ++j)
-          if (F::template same<MODE>(a, xyz2 + (b * M + j) * 3, key)) { ix = (int32_t)j; break; }
+        const T q[3] = {a[0], a[1], a[2]};
+        ix = find_in_chunk<T, MODE, ROWCH, true>(q, xyz2 + b * M * 3, base,
+                                                 min64(M, (int64_t)base + ROWCH), key);
         dv = F::value(key);
       }
       if (dist1) dist1[o] = dv;
@@ -501,10 +525,9 @@ __global__ void chamfer_finalize_kernel(const T* __restrict__ xyz1, const T* __r
       if (N > 0 && !F::empty(key)) {
         const unsigned base = F::chunk(key);
         const T* c = xyz2 + o * 3;
-        ix = (int32_t)base;
-        const int64_t end = min64(N, (int64_t)base + col_chunk);
-        for (int64_t i = base; i < end; ++i)
-          if (F::template same<MODE>(xyz1 + (b * N + i) * 3, c, key)) { ix = (int32_t)i; break; }
+        const T q[3] = {c[0], c[1], c[2]};
+        ix = find_in_chunk<T, MODE, COLCH, false>(q, xyz1 + b * N * 3, base,
+                                                  min64(N, (int64_t)base + COLCH), key);
         dv = F::value(key);
       }
       if (dist2) dist2[o] = dv;
@@ -530,7 +553,8 @@ __global__ void chamfer_finalize_kernel(const T* __restrict__ xyz1, const T* __r
     fl.partials[2 * blockIdx.x] = a;
     fl.partials[2 * blockIdx.x + 1] = c;
     __threadfence();
-    last = atomicAdd(fl.counter, 1u) == gridDim.x - 1;
+    // the counter starts at 0xffffffff (it shares the keys' 0xff fill)
+    last = atomicAdd(fl.counter, 1u) == gridDim.x - 2u;
   }
   __syncthreads();
   if (!last) return;
@@ -648,9 +672,9 @@ int launch_keys_generic(const T* x1, const T* x2, int64_t B, int64_t N, int64_t 
   return check_launch();
 }
 
-template <typename T, int MODE>
+template <typename T, int MODE, int ROWCH, int COLCH>
 int launch_finalize(const T* x1, const T* x2, int64_t B, int64_t N, int64_t M, int64_t rb0,
-                    int64_t rb1, int row_chunk, int col_chunk, const void* k1, const void* k2,
+                    int64_t rb1, const void* k1, const void* k2,
                     T* d1, int32_t* i1, T* d2, int32_t* i2, bool do_cols, T* loss,
                     int reduction, void* loss_ws, cudaStream_t st) {
   const int64_t total = B * (rb1 - rb0) + (do_cols ? B * M : 0);
@@ -663,8 +687,8 @@ int launch_finalize(const T* x1, const T* x2, int64_t B, int64_t N, int64_t M, i
   fl.reduction = reduction;
   fl.partials = (double*)loss_ws;
   fl.counter = loss_ws ? (unsigned*)((char*)loss_ws + kFinPartialBytes) : nullptr;
-  chamfer_finalize_kernel<T, MODE><<<(unsigned)blocks, threads, 0, st>>>(
-      x1, x2, B, N, M, rb0, rb1, row_chunk, col_chunk, (const typename FinTraits<T>::K*)k1,
+  chamfer_finalize_kernel<T, MODE, ROWCH, COLCH><<<(unsigned)blocks, threads, 0, st>>>(
+      x1, x2, B, N, M, rb0, rb1, (const typename FinTraits<T>::K*)k1,
       (const typename FinTraits<T>::K*)k2, d1, i1, d2, i2, do_cols, fl);
   return check_launch();
 }
@@ -694,7 +718,7 @@ int chamfer_finalize(int dtype, int flags, const void* x1, const void* x2, int64
                      void* loss_ws, cudaStream_t st) {
   const bool exact = (flags & TPO_ROUND_EXACT) != 0;
 #define TPO_FIN(T, MODE, CH, CC)                                                                 \
-  launch_finalize<T, MODE>((const T*)x1, (const T*)x2, B, N, M, rb0, rb1, CH, CC, k1, k2, (T*)d1, \
+  launch_finalize<T, MODE, CH, CC>((const T*)x1, (const T*)x2, B, N, M, rb0, rb1, k1, k2, (T*)d1, \
                            i1, (T*)d2, i2, do_cols, (T*)loss, reduction, loss_ws, st)
   switch (dtype) {
     case TPO_F32:

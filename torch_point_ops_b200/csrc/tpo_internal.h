@@ -19,7 +19,7 @@ int chamfer_fwd_keys(int dtype, int flags, const void* x1, const void* x2, int64
                      int64_t M, int64_t rb0, int64_t rb1, void* k1, void* k2, cudaStream_t st);
 // Finalize keys into (dist, idx).  do_cols: also the column side.  loss != null:
 // fused reduction (0 = mean(d1)+mean(d2), 1 = sums) using loss_ws
-// (kFinLossWorkspace bytes, the counter word at kFinPartialBytes zeroed).
+// (kFinLossWorkspace bytes, the counter word at kFinPartialBytes set to 0xffffffff).
 constexpr int kFinMaxBlocks = 148 * 32;
 constexpr size_t kFinPartialBytes = (size_t)kFinMaxBlocks * 2 * sizeof(double);
 constexpr size_t kFinLossWorkspace = kFinPartialBytes + 256;
