@@ -1,0 +1,65 @@
+"""Row-sharded chamfer for one huge cloud pair over several GPUs (one process per
+GPU, torch.distributed over NCCL).
+
+Rank r owns rows [r0, r1) of xyz1 (row_range) and evaluates them against all of
+xyz2.  Its row results are complete; its column results are partial minima.
+Column keys -- (distance bits << 32) | candidate chunk, an int64 >= 0 because
+distances are non-negative -- are merged with ONE all_reduce(MIN), the only
+exchange of the forward.  The backward accumulates the rank's own rows and its
+column shard [c0, c1) (col_range) into full-size gradient buffers, merged with
+an all_reduce(SUM).  Both clouds are replicated on every rank (12 MB fp32 at
+1M points each), so no point data crosses NVLink.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+
+
+def row_range(n: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous, balanced [begin, end) share of n items for `rank`."""
+    return (n * rank) // world, (n * (rank + 1)) // world
+
+
+col_range = row_range
+
+
+def sharded_chamfer_loss(xyz1: torch.Tensor, xyz2: torch.Tensor, group=None, flags: int = 0):
+    """mean(dist1) + mean(dist2) over the full clouds, computed row-sharded.
+
+    Returns (loss, grad_xyz1, grad_xyz2) -- the loss value and its gradients,
+    identical on every rank (forward and backward fused, as a training step uses
+    them).  xyz1 (B,N,3), xyz2 (B,M,3): the full clouds, replicated per rank."""
+    ops = _lib.chamfer_ops
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    xyz1 = xyz1.contiguous()
+    xyz2 = xyz2.contiguous()
+    B, N, M = xyz1.shape[0], xyz1.shape[1], xyz2.shape[1]
+    r0, r1 = row_range(N, world, rank)
+    c0, c1 = col_range(M, world, rank)
+    k1 = ops.chamfer_keys_empty(xyz1, B * N)
+    k2 = ops.chamfer_keys_empty(xyz1, B * M)
+    ops.chamfer_fwd_keys(xyz1, xyz2, r0, r1, flags, k1, k2)
+    if world > 1:
+        if k2.numel() != B * M:
+            raise NotImplementedError("sharded fp64 chamfer needs 128-bit key merging")
+        dist.all_reduce(k2, op=dist.ReduceOp.MIN, group=group)
+    d1, d2, i1, i2 = ops.chamfer_finalize(xyz1, xyz2, r0, r1, flags, k1, k2)
+    # loss: this rank's rows of dist1 + its column shard of dist2, summed over ranks
+    part = d1[:, r0:r1].double().sum() / (B * N) + d2[:, c0:c1].double().sum() / (B * M)
+    # backward of the mean: 1/(B*N) per row, 1/(B*M) per column
+    g1 = torch.full((B, N), 1.0 / (B * N), dtype=xyz1.dtype, device=xyz1.device)
+    g2 = torch.full((B, M), 1.0 / (B * M), dtype=xyz1.dtype, device=xyz1.device)
+    gx1 = torch.zeros_like(xyz1)
+    gx2 = torch.zeros_like(xyz2)
+    ops.chamfer_bwd_partial(xyz1, xyz2, r0, r1, c0, c1, i1, i2, g1, g2, gx1, gx2)
+    if world > 1:
+        dist.all_reduce(part, group=group)
+        flat = torch.cat([gx1.view(-1), gx2.view(-1)])
+        dist.all_reduce(flat, group=group)
+        gx1 = flat[: gx1.numel()].view_as(gx1)
+        gx2 = flat[gx1.numel():].view_as(gx2)
+    return part.to(xyz1.dtype), gx1, gx2
