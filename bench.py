@@ -349,11 +349,27 @@ def kernel_roofline(cfg, inputs, dev, clocks, reps=20, rows=None):
            "peak": round(peak, 1), "unit": "Gpair/s", "frac": round(achieved / peak, 4),
            "peak_basis": "nominal FP32 pipe: 148 SM x 128 lanes x 1965 MHz / 6 instr per pair "
                          "(MEASURED_PEAKS.json has no FP32 figure)",
-           "kernel_ms": round(ms, 4), "traffic": None}
+           "kernel_ms": round(ms, 4), "traffic": profiled_traffic(cfg)}
     if clocks.get("sm_mhz"):
         p2 = SMS * FP32_LANES * clocks["sm_mhz"] * 1e6 / INSTR_PER_PAIR / 1e9
         out["frac_at_measured_clock"] = round(achieved / p2, 4)
     return out
+
+
+def profiled_traffic(cfg):
+    """DRAM bytes per launch of the keys kernel from the committed ncu summary
+    (profiles/chamfer_keys_f32_config<N>.md), or None when none was captured."""
+    name = {"Chamfer fwd+bwd B=32 N=M=2048 fp32 sphere+noise (config 2)": "2"}.get(cfg["desc"])
+    if name is None:
+        return None
+    path = os.path.join(ROOT, "profiles", f"chamfer_keys_f32_config{name}.md")
+    try:
+        for line in open(path):
+            if line.startswith("| dram_bytes_per_launch"):
+                return int(line.split("|")[2].strip())
+    except OSError:
+        pass
+    return None
 
 
 # ------------------------------------------------------ CPU reference path ----
