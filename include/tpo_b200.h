@@ -132,21 +132,22 @@ TPO_API int tpo_chamfer_bwd_partial(int dtype, const void* xyz1, const void* xyz
 
 /* Fused ChamferDistance loss (chamfer/chamfer.py:18-23: reduction "mean" ->
  * mean(dist1) + mean(dist2), "sum" -> sum(dist1) + sum(dist2)).  Replaces the
- * reference's chamfer_forward + two torch reductions with the forward kernels
- * plus an in-kernel, deterministic (fixed-order) reduction; writes the scalar
- * `loss` (1 element, dtype) and the argmin indices needed by the backward.
- * The backward reads the scalar grad_loss from device memory and applies the
- * reduction's scaling inside the scatter kernel (no expanded per-point grads).
- * Workspace: tpo_chamfer_loss_workspace_size() bytes, 256-byte aligned. */
+ * reference's chamfer_forward + two torch reductions + the expanded per-point
+ * gradients of its backward.  The forward writes the scalar `loss` (1 element,
+ * dtype); for fp32 the reduction runs inside the distance kernel itself
+ * (deterministic, fixed order).  Everything the backward needs stays in
+ * `workspace` (tpo_chamfer_loss_workspace_size() bytes, 256-byte aligned): pass
+ * the same, unmodified workspace and the same inputs/flags to the backward,
+ * which reads the scalar grad_loss from device memory and applies the
+ * reduction's scaling inside the scatter kernel. */
 enum tpo_reduction { TPO_REDUCE_MEAN = 0, TPO_REDUCE_SUM = 1 };
 TPO_API size_t tpo_chamfer_loss_workspace_size(int dtype, int64_t B, int64_t N, int64_t M);
 TPO_API int tpo_chamfer_loss_fwd(int dtype, int flags, const void* xyz1, const void* xyz2,
                                  int64_t B, int64_t N, int64_t M, int reduction, void* loss,
-                                 int32_t* idx1, int32_t* idx2, void* workspace,
-                                 size_t workspace_bytes, void* stream);
-TPO_API int tpo_chamfer_loss_bwd(int dtype, const void* xyz1, const void* xyz2, int64_t B,
-                                 int64_t N, int64_t M, int reduction, const int32_t* idx1,
-                                 const int32_t* idx2, const void* grad_loss, void* grad_xyz1,
+                                 void* workspace, size_t workspace_bytes, void* stream);
+TPO_API int tpo_chamfer_loss_bwd(int dtype, int flags, const void* xyz1, const void* xyz2,
+                                 int64_t B, int64_t N, int64_t M, int reduction,
+                                 const void* workspace, const void* grad_loss, void* grad_xyz1,
                                  void* grad_xyz2, void* stream);
 
 /* ------------------------------------------------------------------------- */

@@ -110,28 +110,27 @@ def gather_bwd(gout, idx, lengths, M):
 
 
 def chamfer_loss_fwd(x1, x2, reduction=0, flags=0):
+    """Returns (loss, state); state is the workspace the backward consumes."""
     B, N, _ = x1.shape
     M = x2.shape[1]
     dt = DT[x1.dtype]
     loss = torch.empty((), dtype=x1.dtype, device=x1.device)
-    i1 = torch.empty(B, N, dtype=torch.int32, device=x1.device)
-    i2 = torch.empty(B, M, dtype=torch.int32, device=x1.device)
     lib().tpo_chamfer_loss_workspace_size.restype = ctypes.c_size_t
     lib().tpo_chamfer_loss_workspace_size.argtypes = [ctypes.c_int, I64, I64, I64]
     n = lib().tpo_chamfer_loss_workspace_size(dt, B, N, M)
     ws = torch.empty(n, dtype=torch.uint8, device=x1.device)
     check(lib().tpo_chamfer_loss_fwd(dt, flags, p(x1), p(x2), I64(B), I64(N), I64(M),
-                                     ctypes.c_int(reduction), p(loss), p(i1), p(i2), p(ws),
-                                     ctypes.c_size_t(n), stream()))
-    return loss, i1, i2
+                                     ctypes.c_int(reduction), p(loss), p(ws), ctypes.c_size_t(n),
+                                     stream()))
+    return loss, ws
 
 
-def chamfer_loss_bwd(x1, x2, i1, i2, grad_loss, reduction=0):
+def chamfer_loss_bwd(x1, x2, state, grad_loss, reduction=0, flags=0):
     B, N, _ = x1.shape
     M = x2.shape[1]
     gx1 = torch.empty_like(x1)
     gx2 = torch.empty_like(x2)
-    check(lib().tpo_chamfer_loss_bwd(DT[x1.dtype], p(x1), p(x2), I64(B), I64(N), I64(M),
-                                     ctypes.c_int(reduction), p(i1), p(i2), p(grad_loss), p(gx1),
+    check(lib().tpo_chamfer_loss_bwd(DT[x1.dtype], flags, p(x1), p(x2), I64(B), I64(N), I64(M),
+                                     ctypes.c_int(reduction), p(state), p(grad_loss), p(gx1),
                                      p(gx2), stream()))
     return gx1, gx2

@@ -55,18 +55,19 @@ def _(xyz1, xyz2, idx1, idx2, grad_dist1, grad_dist2):
 
 
 def _loss_setup(ctx, inputs, output):
-    xyz1, xyz2, reduction = inputs[0], inputs[1], inputs[2]
-    _, idx1, idx2 = output
-    ctx.save_for_backward(xyz1, xyz2, idx1, idx2)
+    xyz1, xyz2, reduction, flags = inputs
+    _, state = output
+    ctx.save_for_backward(xyz1, xyz2, state)
     ctx.reduction = reduction
-    ctx.set_materialize_grads(False)  # no zero tensors for the int outputs' grads
+    ctx.flags = flags
+    ctx.set_materialize_grads(False)
 
 
-def _loss_backward(ctx, grad_loss, gi1, gi2):
-    xyz1, xyz2, idx1, idx2 = ctx.saved_tensors
+def _loss_backward(ctx, grad_loss, grad_state):
+    xyz1, xyz2, state = ctx.saved_tensors
     if grad_loss is None:
         return None, None, None, None
-    gx1, gx2 = _ops.chamfer_loss_backward(xyz1, xyz2, idx1, idx2, grad_loss, ctx.reduction)
+    gx1, gx2 = _ops.chamfer_loss_backward(xyz1, xyz2, state, grad_loss, ctx.reduction, ctx.flags)
     return gx1, gx2, None, None
 
 
@@ -76,14 +77,13 @@ torch.library.register_autograd(
 
 @torch.library.register_fake("torch_point_ops_b200_chamfer::chamfer_loss")
 def _(xyz1, xyz2, reduction, flags):
-    b, n, _ = xyz1.shape
-    m = xyz2.shape[1]
-    return (xyz1.new_empty(()), xyz1.new_empty(b, n, dtype=torch.int32),
-            xyz1.new_empty(b, m, dtype=torch.int32))
+    ctx = torch.library.get_ctx()
+    n = ctx.new_dynamic_size()
+    return xyz1.new_empty(()), xyz1.new_empty(n, dtype=torch.uint8)
 
 
 @torch.library.register_fake("torch_point_ops_b200_chamfer::chamfer_loss_backward")
-def _(xyz1, xyz2, idx1, idx2, grad_loss, reduction):
+def _(xyz1, xyz2, state, grad_loss, reduction, flags):
     return torch.empty_like(xyz1), torch.empty_like(xyz2)
 
 
@@ -92,7 +92,7 @@ def chamfer_loss(xyz1: torch.Tensor, xyz2: torch.Tensor, reduction: str = "mean"
     sum(dist1) + sum(dist2) ("sum"), computed inside the forward kernels (no
     per-point distance tensors, no separate reduction launches); autograd-aware."""
     red = {"mean": 0, "sum": 1}[reduction]
-    loss, _, _ = _ops.chamfer_loss(xyz1, xyz2, red, _lib.rounding_flags())
+    loss, _ = _ops.chamfer_loss(xyz1, xyz2, red, _lib.rounding_flags())
     return loss
 
 

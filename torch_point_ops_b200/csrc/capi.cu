@@ -163,54 +163,89 @@ int tpo_chamfer_bwd_partial(int dtype, const void* xyz1, const void* xyz2, int64
                                 grad_xyz2, (cudaStream_t)stream);
 }
 
+// Fused-loss workspace: everything the backward needs stays in it.
+//   [keys1|keys2][keys-loss counters|batch partials][finalize partials|counter][idx1][idx2]
+// fp32 with a non-empty problem uses the keys kernel's fused reduction and the
+// backward re-derives the neighbours from the keys; other cases finalize into
+// idx1/idx2 and reduce there.
+struct LossLayout {
+  size_t keys, kl, fin, idx1, idx2, total;
+};
+static LossLayout loss_layout(int dtype, int64_t B, int64_t N, int64_t M) {
+  LossLayout L;
+  L.keys = 0;
+  L.kl = tpo_chamfer_fwd_workspace_size(dtype, B, N, M);
+  L.fin = L.kl + keys_loss_bytes(B);
+  L.idx1 = L.fin + align256(kFinLossWorkspace);
+  L.idx2 = L.idx1 + align256(4 * (size_t)B * (size_t)N);
+  L.total = L.idx2 + align256(4 * (size_t)B * (size_t)M);
+  return L;
+}
+static bool loss_uses_keys_kernel(int dtype, int64_t B, int64_t N, int64_t M) {
+  return dtype == TPO_F32 && B > 0 && N > 0 && M > 0;
+}
+
 size_t tpo_chamfer_loss_workspace_size(int dtype, int64_t B, int64_t N, int64_t M) {
   if (!valid_dtype(dtype) || B < 0 || N < 0 || M < 0) return 0;
-  return tpo_chamfer_fwd_workspace_size(dtype, B, N, M) + align256(kFinLossWorkspace);
+  return loss_layout(dtype, B, N, M).total;
 }
 
 int tpo_chamfer_loss_fwd(int dtype, int flags, const void* xyz1, const void* xyz2, int64_t B,
-                         int64_t N, int64_t M, int reduction, void* loss, int32_t* idx1,
-                         int32_t* idx2, void* workspace, size_t workspace_bytes, void* stream) {
+                         int64_t N, int64_t M, int reduction, void* loss, void* workspace,
+                         size_t workspace_bytes, void* stream) {
   int s = check_chamfer_shape(dtype, xyz1, xyz2, B, N, M);
   if (s) return s;
   if (reduction != TPO_REDUCE_MEAN && reduction != TPO_REDUCE_SUM)
     return fail(TPO_ERR_INVALID_ARGUMENT, "chamfer_loss: reduction must be TPO_REDUCE_MEAN or TPO_REDUCE_SUM");
-  if (!loss || (B * N > 0 && !idx1) || (B * M > 0 && !idx2))
-    return fail(TPO_ERR_INVALID_ARGUMENT, "chamfer_loss: null output");
-  const size_t need = tpo_chamfer_loss_workspace_size(dtype, B, N, M);
-  if (!workspace || workspace_bytes < need || (uintptr_t)workspace % 256)
+  if (!loss) return fail(TPO_ERR_INVALID_ARGUMENT, "chamfer_loss: null loss");
+  const LossLayout L = loss_layout(dtype, B, N, M);
+  if (!workspace || workspace_bytes < L.total || (uintptr_t)workspace % 256)
     return fail(TPO_ERR_WORKSPACE, "chamfer_loss: workspace missing, unaligned or smaller than tpo_chamfer_loss_workspace_size()");
   cudaStream_t st = (cudaStream_t)stream;
+  char* w = (char*)workspace;
   const size_t kb = (size_t)tpo_chamfer_key_bytes(dtype);
-  const size_t keys_bytes = tpo_chamfer_fwd_workspace_size(dtype, B, N, M);
-  char* k1 = (char*)workspace;
+  char* k1 = w;
   char* k2 = k1 + align256(kb * (size_t)B * (size_t)N);
-  char* lw = k1 + keys_bytes;
-  // one fill: keys to the empty key, the finalize counter (after the partials) to 0xffffffff
-  if ((s = cuda_status(cudaMemsetAsync(workspace, 0xff, need, st)))) return s;
+  if (loss_uses_keys_kernel(dtype, B, N, M)) {
+    // keys to the empty key and the reduction counters to 0xffffffff: one fill
+    if ((s = cuda_status(cudaMemsetAsync(w, 0xff, L.kl + keys_loss_counter_bytes(B), st)))) return s;
+    return chamfer_loss_keys_f32(flags, xyz1, xyz2, B, N, M, reduction, k1, k2, w + L.kl, loss, st);
+  }
+  if (L.kl && (s = cuda_status(cudaMemsetAsync(w, 0xff, L.kl, st)))) return s;
+  if ((s = cuda_status(cudaMemsetAsync(w + L.fin + kFinPartialBytes, 0xff, 256, st)))) return s;
   if (B > 0 && N > 0 && M > 0 &&
       (s = chamfer_fwd_keys(dtype, flags, xyz1, xyz2, B, N, M, 0, N, k1, k2, st)))
     return s;
-  return chamfer_finalize(dtype, flags, xyz1, xyz2, B, N, M, 0, N, k1, k2, nullptr, idx1, nullptr,
-                          idx2, true, loss, reduction, lw, st);
+  return chamfer_finalize(dtype, flags, xyz1, xyz2, B, N, M, 0, N, k1, k2, nullptr,
+                          (int32_t*)(w + L.idx1), nullptr, (int32_t*)(w + L.idx2), true, loss,
+                          reduction, w + L.fin, st);
 }
 
-int tpo_chamfer_loss_bwd(int dtype, const void* xyz1, const void* xyz2, int64_t B, int64_t N,
-                         int64_t M, int reduction, const int32_t* idx1, const int32_t* idx2,
+int tpo_chamfer_loss_bwd(int dtype, int flags, const void* xyz1, const void* xyz2, int64_t B,
+                         int64_t N, int64_t M, int reduction, const void* workspace,
                          const void* grad_loss, void* grad_xyz1, void* grad_xyz2, void* stream) {
   int s = check_chamfer_shape(dtype, xyz1, xyz2, B, N, M);
   if (s) return s;
   if (reduction != TPO_REDUCE_MEAN && reduction != TPO_REDUCE_SUM)
     return fail(TPO_ERR_INVALID_ARGUMENT, "chamfer_loss_bwd: bad reduction");
-  if (!grad_loss || (B * N > 0 && (!grad_xyz1 || !idx1)) || (B * M > 0 && (!grad_xyz2 || !idx2)))
+  if (!grad_loss || !workspace || (B * N > 0 && !grad_xyz1) || (B * M > 0 && !grad_xyz2))
     return fail(TPO_ERR_INVALID_ARGUMENT, "chamfer_loss_bwd: null pointer");
   cudaStream_t st = (cudaStream_t)stream;
   const size_t es = (size_t)dtype_size(dtype);
   if (B * N > 0 && (s = cuda_status(cudaMemsetAsync(grad_xyz1, 0, es * 3 * B * N, st)))) return s;
   if (B * M > 0 && (s = cuda_status(cudaMemsetAsync(grad_xyz2, 0, es * 3 * B * M, st)))) return s;
-  return chamfer_bwd_accumulate(dtype, xyz1, xyz2, B, N, M, 0, N, 0, M, idx1, idx2, nullptr,
-                                nullptr, grad_loss, reduction == TPO_REDUCE_MEAN ? 1 : 2,
-                                grad_xyz1, grad_xyz2, st);
+  const LossLayout L = loss_layout(dtype, B, N, M);
+  const char* w = (const char*)workspace;
+  if (loss_uses_keys_kernel(dtype, B, N, M)) {
+    const size_t kb = (size_t)tpo_chamfer_key_bytes(dtype);
+    return chamfer_bwd_from_keys_f32(flags, xyz1, xyz2, B, N, M, w,
+                                     w + align256(kb * (size_t)B * (size_t)N), grad_loss,
+                                     reduction, grad_xyz1, grad_xyz2, st);
+  }
+  return chamfer_bwd_accumulate(dtype, xyz1, xyz2, B, N, M, 0, N, 0, M,
+                                (const int32_t*)(w + L.idx1), (const int32_t*)(w + L.idx2),
+                                nullptr, nullptr, grad_loss,
+                                reduction == TPO_REDUCE_MEAN ? 1 : 2, grad_xyz1, grad_xyz2, st);
 }
 
 static int check_knn(int dtype, const void* p1, const void* p2, int64_t N, int64_t P1, int64_t P2,

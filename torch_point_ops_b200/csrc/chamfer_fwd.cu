@@ -66,12 +66,96 @@ __device__ __forceinline__ float col_min(const float* v) {
   }
 }
 
+// Fused ChamferDistance reduction inside the keys kernel: the last CTA of each
+// batch (per-batch counter) sums that batch's final keys -- their high words are
+// the distances -- in a fixed order, and the last batch folds the per-batch sums
+// in batch order.  Deterministic; counters start at 0xffffffff.
+struct KeysLoss {
+  unsigned* batch_ctr;  // [B]
+  unsigned* glob_ctr;   // [1]
+  double* batch_part;   // [2B]
+  float* loss;          // nullptr: no fused loss
+  int reduction;        // 0 mean(d1)+mean(d2), 1 sum(d1)+sum(d2)
+};
+
+__device__ __forceinline__ void block_sum2(double& a, double& c, double* sa, double* sc) {
+#pragma unroll
+  for (int off = 16; off; off >>= 1) {
+    a += __shfl_down_sync(0xffffffffu, a, off);
+    c += __shfl_down_sync(0xffffffffu, c, off);
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) { sa[warp] = a; sc[warp] = c; }
+  __syncthreads();
+  a = 0.0;
+  c = 0.0;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) { a += sa[w]; c += sc[w]; }
+}
+
+// Sum of the distances held in n keys by this block, in a fixed order: 8
+// independent loads in flight per thread (the loads, not the adds, set the time).
+__device__ __forceinline__ double sum_key_values(const u64* k, int64_t n) {
+  constexpr int U = 8;
+  double acc[U];
+#pragma unroll
+  for (int u = 0; u < U; ++u) acc[u] = 0.0;
+  const int64_t stride = (int64_t)blockDim.x * U;
+  for (int64_t i0 = threadIdx.x; i0 < n; i0 += stride) {
+    u64 v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t i = i0 + (int64_t)u * blockDim.x;
+      v[u] = i < n ? __ldcg(k + i) : 0ull;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) acc[u] += (double)__uint_as_float((unsigned)(v[u] >> 32));
+  }
+  double t = 0.0;
+#pragma unroll
+  for (int u = 0; u < U; ++u) t += acc[u];
+  return t;
+}
+
+__device__ void keys_loss_epilogue(const KeysLoss& kl, const u64* keys1, const u64* keys2,
+                                   int64_t b, int64_t B, int64_t N, int64_t M, int per_batch) {
+  __shared__ double sa[CF_MAXW], sc[CF_MAXW];
+  __shared__ bool s_last;
+  __threadfence();  // this thread's key reductions before the counter
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(kl.batch_ctr + b, 1u) == (unsigned)(per_batch - 2);
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  double a = sum_key_values(keys1 + b * N, N), c = sum_key_values(keys2 + b * M, M);
+  block_sum2(a, c, sa, sc);
+  __shared__ bool s_glob;
+  if (threadIdx.x == 0) {
+    __stcg(kl.batch_part + 2 * b, a);
+    __stcg(kl.batch_part + 2 * b + 1, c);
+    __threadfence();
+    s_glob = atomicAdd(kl.glob_ctr, 1u) == (unsigned)(B - 2);
+  }
+  __syncthreads();
+  if (!s_glob || threadIdx.x != 0) return;
+  __threadfence();
+  double ta = 0.0, tc = 0.0;
+  for (int64_t k = 0; k < B; ++k) {
+    ta += __ldcg(kl.batch_part + 2 * k);
+    tc += __ldcg(kl.batch_part + 2 * k + 1);
+  }
+  // torch semantics: each mean (or sum) rounded to float, then added in float
+  const float t1 = kl.reduction == 0 ? (float)(ta / (double)(B * N)) : (float)ta;
+  const float t2 = kl.reduction == 0 ? (float)(tc / (double)(B * M)) : (float)tc;
+  *kl.loss = __fadd_rn(t1, t2);
+}
+
 template <int MODE>
 __global__ void __launch_bounds__(CF_MAXW * 32, TPO_CF_MINB)
     chamfer_keys_f32_kernel(const float* __restrict__ xyz1, const float* __restrict__ xyz2,
                             int64_t N, int64_t M, int64_t row_begin, int64_t row_end,
                             int rb_count, int cs_count, int64_t seg,
-                            u64* __restrict__ keys1, u64* __restrict__ keys2) {
+                            u64* __restrict__ keys1, u64* __restrict__ keys2, KeysLoss kl) {
   __shared__ __align__(16) float2 s_col[CF_TILE_STEPS][3][CF_C];
   __shared__ __align__(16) uint2 s_wb[CF_MAXW][CF_TILE];  // {ballot, distance bits}
 
@@ -92,21 +176,24 @@ __global__ void __launch_bounds__(CF_MAXW * 32, TPO_CF_MINB)
   const int n_active = (int)min64(W, (row_end - blk_row0 + CF_ROWS_PER_WARP - 1) / CF_ROWS_PER_WARP);
   const float qnan = __int_as_float(0x7fffffff);
 
+  // The CTA's rows, staged once (coalesced) in shared memory: lanes read their
+  // R rows from here, and the column merge rescans winning row chunks here.
+  __shared__ __align__(16) float s_rows[CF_MAXW * CF_ROWS_PER_WARP * 3];
+  {
+    const int64_t nrow = min64((int64_t)W * CF_ROWS_PER_WARP, max64(row_end - blk_row0, 0));
+    const float* src = xyz1 + (b * N + blk_row0) * 3;
+    for (int e = threadIdx.x; e < W * CF_ROWS_PER_WARP * 3; e += blockDim.x)
+      s_rows[e] = e < nrow * 3 ? __ldg(src + e) : qnan;
+  }
+  __syncthreads();
   u64 QX[CF_RP], QY[CF_RP], QZ[CF_RP];
   {
-    const float* a = xyz1 + (b * N + lane_row0) * 3;
+    const float* a = s_rows + (warp * CF_ROWS_PER_WARP + lane * CF_R) * 3;
 #pragma unroll
     for (int p = 0; p < CF_RP; ++p) {
-      float v[6];
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const bool ok = lane_row0 + 2 * p + h < row_end;
-#pragma unroll
-        for (int d = 0; d < 3; ++d) v[h * 3 + d] = ok ? __ldg(a + (2 * p + h) * 3 + d) : qnan;
-      }
-      QX[p] = pk(v[0], v[3]);
-      QY[p] = pk(v[1], v[4]);
-      QZ[p] = pk(v[2], v[5]);
+      QX[p] = pk(a[6 * p + 0], a[6 * p + 3]);
+      QY[p] = pk(a[6 * p + 1], a[6 * p + 4]);
+      QZ[p] = pk(a[6 * p + 2], a[6 * p + 5]);
     }
   }
   float best[CF_R];
@@ -179,17 +266,28 @@ __global__ void __launch_bounds__(CF_MAXW * 32, TPO_CF_MINB)
       }
     }
     __syncthreads();
-    // merge the warps' column results (lowest row chunk on equal distance) and
-    // fold them into the global keys
+    // merge the warps' column results: the smallest distance, lowest warp (= lowest
+    // rows) on ties; then rescan the winning lane's R rows in shared memory with
+    // the identical arithmetic, so the key carries the exact lowest row index
     for (int col = threadIdx.x; col < ncols; col += blockDim.x) {
-      u64 k = ~0ull;
-      for (int w = 0; w < n_active; ++w) {
-        const uint2 e = s_wb[w][col];
-        const unsigned win = __ffs(e.x) - 1;
-        const u64 kw = ((u64)e.y << 32) |
-                       (unsigned)(blk_row0 + (int64_t)w * CF_ROWS_PER_WARP + (int64_t)win * CF_R);
-        k = min(k, kw);
+      unsigned bw = s_wb[0][col].y;
+      int wb = 0;
+      for (int w = 1; w < n_active; ++w) {
+        const unsigned v = s_wb[w][col].y;
+        if (v < bw) { bw = v; wb = w; }
       }
+      const int lr0 = wb * CF_ROWS_PER_WARP + (__ffs(s_wb[wb][col].x) - 1) * CF_R;
+      const float cx = s_col[col >> 2][0][col & 3].x;
+      const float cy = s_col[col >> 2][1][col & 3].x;
+      const float cz = s_col[col >> 2][2][col & 3].x;
+      int found = 0;
+#pragma unroll
+      for (int k = CF_R - 1; k >= 0; --k) {
+        const float* r = s_rows + (lr0 + k) * 3;
+        const float dd = dist1f<MODE>(__fsub_rn(cx, r[0]), __fsub_rn(cy, r[1]), __fsub_rn(cz, r[2]));
+        if (__float_as_uint(dd) == bw) found = k;
+      }
+      const u64 k = ((u64)bw << 32) | (unsigned)(blk_row0 + lr0 + found);
       red_min_u64(keys2 + b * M + tc + col, k);
     }
   }
@@ -202,6 +300,9 @@ __global__ void __launch_bounds__(CF_MAXW * 32, TPO_CF_MINB)
                     ((u64)__float_as_uint(best[r]) << 32) | (unsigned)bchunk[r]);
     }
   }
+  if (kl.loss != nullptr)
+    keys_loss_epilogue(kl, keys1, keys2, b, (int64_t)gridDim.x / (rb_count * cs_count), N, M,
+                       rb_count * cs_count);
 }
 
 // ------------------------- fp16 / fp64 generic path -------------------------
@@ -525,9 +626,13 @@ __global__ void chamfer_finalize_kernel(const T* __restrict__ xyz1, const T* __r
       if (N > 0 && !F::empty(key)) {
         const unsigned base = F::chunk(key);
         const T* c = xyz2 + o * 3;
-        const T q[3] = {c[0], c[1], c[2]};
-        ix = find_in_chunk<T, MODE, COLCH, false>(q, xyz1 + b * N * 3, base,
-                                                  min64(N, (int64_t)base + COLCH), key);
+        if constexpr (COLCH == 1) {
+          ix = (int32_t)base;  // the keys kernel already stored the exact row
+        } else {
+          const T q[3] = {c[0], c[1], c[2]};
+          ix = find_in_chunk<T, MODE, COLCH, false>(q, xyz1 + b * N * 3, base,
+                                                    min64(N, (int64_t)base + COLCH), key);
+        }
         dv = F::value(key);
       }
       if (dist2) dist2[o] = dv;
@@ -589,6 +694,53 @@ __global__ void chamfer_finalize_kernel(const T* __restrict__ xyz1, const T* __r
   *fl.loss = FinRound<T>::add(t1, t2);
 }
 
+// Backward of the fused loss straight from the forward's keys (fp32): each point
+// resolves its neighbour by rescanning its key's chunk (as the finalize kernel
+// does), then scatters (2g)(p - q) like chamfer_bwd_kernel, with g the loss
+// gradient scaled as torch's MeanBackward does (g / count) or unscaled (sum).
+template <int MODE>
+__global__ void chamfer_bwd_from_keys_f32_kernel(const float* __restrict__ xyz1,
+                                                 const float* __restrict__ xyz2, int64_t B,
+                                                 int64_t N, int64_t M,
+                                                 const u64* __restrict__ keys1,
+                                                 const u64* __restrict__ keys2,
+                                                 const float* __restrict__ grad_loss,
+                                                 int reduction, float* __restrict__ gx1,
+                                                 float* __restrict__ gx2) {
+  const float g = *grad_loss;
+  const float g1 = __fmul_rn(reduction == 0 ? __fdiv_rn(g, (float)(B * N)) : g, 2.0f);
+  const float g2 = __fmul_rn(reduction == 0 ? __fdiv_rn(g, (float)(B * M)) : g, 2.0f);
+  const int64_t n1 = B * N;
+  const int64_t total = n1 + B * M;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const bool row = t < n1;
+    const int64_t u = row ? t : t - n1;
+    const int64_t P = row ? N : M, Q = row ? M : N;
+    const int64_t b = u / P;
+    const u64 key = row ? __ldg(keys1 + u) : __ldg(keys2 + u);
+    if (Q == 0 || key == ~0ull) continue;
+    const float* own = (row ? xyz1 : xyz2) + u * 3;
+    const float* other = (row ? xyz2 : xyz1) + b * Q * 3;
+    const float q[3] = {own[0], own[1], own[2]};
+    const int64_t base = (unsigned)key;
+    // column keys hold the exact row; row keys hold the first column of an 8-column chunk
+    const int32_t j = row ? find_in_chunk<float, MODE, CF_CHUNK, true>(q, other, base,
+                                                                       min64(Q, base + CF_CHUNK), key)
+                          : (int32_t)base;
+    const float gg = row ? g1 : g2;
+    float* ga = (row ? gx1 : gx2) + u * 3;
+    float* gb = (row ? gx2 : gx1) + (b * Q + j) * 3;
+    const float* pb = other + (int64_t)j * 3;
+#pragma unroll
+    for (int d = 0; d < 3; ++d) {
+      const float v = __fmul_rn(gg, __fsub_rn(q[d], pb[d]));
+      atomicAdd(ga + d, v);
+      atomicAdd(gb + d, -v);
+    }
+  }
+}
+
 // ------------------------------- host side -------------------------------
 namespace {
 
@@ -641,7 +793,8 @@ int slots_for(KernelT kernel, int threads) {
 
 template <int MODE>
 int launch_keys_f32(const float* x1, const float* x2, int64_t B, int64_t N, int64_t M,
-                    int64_t rb0, int64_t rb1, void* k1, void* k2, cudaStream_t st) {
+                    int64_t rb0, int64_t rb1, void* k1, void* k2, cudaStream_t st,
+                    KeysLoss kl = KeysLoss{nullptr, nullptr, nullptr, nullptr, 0}) {
   auto kern = chamfer_keys_f32_kernel<MODE>;
   static thread_local int slots_cache[64] = {0};
   int dev = 0;
@@ -651,7 +804,7 @@ int launch_keys_f32(const float* x1, const float* x2, int64_t B, int64_t N, int6
   const Plan p = make_plan(B, rb1 - rb0, M, CF_ROWS_PER_WARP, CF_MAXW, slots);
   if (p.ctas <= 0) return TPO_OK;
   kern<<<(unsigned)p.ctas, p.warps * 32, 0, st>>>(x1, x2, N, M, rb0, rb1, p.rb_count, p.cs_count,
-                                                   p.seg, (u64*)k1, (u64*)k2);
+                                                   p.seg, (u64*)k1, (u64*)k2, kl);
   return check_launch();
 }
 
@@ -722,7 +875,7 @@ int chamfer_finalize(int dtype, int flags, const void* x1, const void* x2, int64
                            i1, (T*)d2, i2, do_cols, (T*)loss, reduction, loss_ws, st)
   switch (dtype) {
     case TPO_F32:
-      return exact ? TPO_FIN(float, TPO_ROUND_EXACT, CF_CHUNK, CF_R) : TPO_FIN(float, TPO_ROUND_FMA, CF_CHUNK, CF_R);
+      return exact ? TPO_FIN(float, TPO_ROUND_EXACT, CF_CHUNK, 1) : TPO_FIN(float, TPO_ROUND_FMA, CF_CHUNK, 1);
     case TPO_F16:
       return TPO_FIN(__half, TPO_ROUND_EXACT, CG_C, CG_R);
     case TPO_F64:
@@ -730,6 +883,39 @@ int chamfer_finalize(int dtype, int flags, const void* x1, const void* x2, int64
   }
 #undef TPO_FIN
   return TPO_ERR_INVALID_ARGUMENT;
+}
+
+int chamfer_loss_keys_f32(int flags, const void* x1, const void* x2, int64_t B, int64_t N,
+                          int64_t M, int reduction, void* k1, void* k2, void* lossws, void* loss,
+                          cudaStream_t st) {
+  KeysLoss kl;
+  kl.batch_ctr = (unsigned*)lossws;
+  kl.glob_ctr = kl.batch_ctr + B;
+  kl.batch_part = (double*)((char*)lossws + keys_loss_counter_bytes(B));
+  kl.loss = (float*)loss;
+  kl.reduction = reduction;
+  const bool exact = (flags & TPO_ROUND_EXACT) != 0;
+  return exact ? launch_keys_f32<TPO_ROUND_EXACT>((const float*)x1, (const float*)x2, B, N, M, 0, N, k1, k2, st, kl)
+               : launch_keys_f32<TPO_ROUND_FMA>((const float*)x1, (const float*)x2, B, N, M, 0, N, k1, k2, st, kl);
+}
+
+int chamfer_bwd_from_keys_f32(int flags, const void* x1, const void* x2, int64_t B, int64_t N,
+                              int64_t M, const void* k1, const void* k2, const void* grad_loss,
+                              int reduction, void* gx1, void* gx2, cudaStream_t st) {
+  const int64_t total = B * (N + M);
+  if (total <= 0) return TPO_OK;
+  const int threads = 256;
+  const unsigned blocks = (unsigned)std::min<int64_t>((total + threads - 1) / threads, 148 * 16);
+  const bool exact = (flags & TPO_ROUND_EXACT) != 0;
+  if (exact)
+    chamfer_bwd_from_keys_f32_kernel<TPO_ROUND_EXACT><<<blocks, threads, 0, st>>>(
+        (const float*)x1, (const float*)x2, B, N, M, (const u64*)k1, (const u64*)k2,
+        (const float*)grad_loss, reduction, (float*)gx1, (float*)gx2);
+  else
+    chamfer_bwd_from_keys_f32_kernel<TPO_ROUND_FMA><<<blocks, threads, 0, st>>>(
+        (const float*)x1, (const float*)x2, B, N, M, (const u64*)k1, (const u64*)k2,
+        (const float*)grad_loss, reduction, (float*)gx1, (float*)gx2);
+  return check_launch();
 }
 
 }  // namespace tpo

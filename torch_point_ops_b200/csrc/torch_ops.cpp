@@ -94,9 +94,9 @@ std::tuple<at::Tensor, at::Tensor> chamfer_backward(const at::Tensor& xyz1_, con
 }
 
 // ---- fused ChamferDistance loss (reduction 0 = mean, 1 = sum) ----
-std::tuple<at::Tensor, at::Tensor, at::Tensor> chamfer_loss(const at::Tensor& xyz1_,
-                                                            const at::Tensor& xyz2_,
-                                                            int64_t reduction, int64_t flags) {
+// Returns (loss, state): `state` is the byte workspace the backward consumes.
+std::tuple<at::Tensor, at::Tensor> chamfer_loss(const at::Tensor& xyz1_, const at::Tensor& xyz2_,
+                                                int64_t reduction, int64_t flags) {
   check_cloud(xyz1_, "xyz1");
   check_cloud(xyz2_, "xyz2");
   TORCH_CHECK(xyz1_.size(2) == 3 && xyz2_.size(2) == 3, "chamfer: points must be 3-D");
@@ -107,32 +107,31 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> chamfer_loss(const at::Tensor& xy
   const int64_t B = xyz1.size(0), N = xyz1.size(1), M = xyz2.size(1);
   const int dt = to_dtype(xyz1);
   auto loss = at::empty({}, xyz1.options());
-  auto idx1 = at::empty({B, N}, xyz1.options().dtype(at::kInt));
-  auto idx2 = at::empty({B, M}, xyz1.options().dtype(at::kInt));
   const size_t ws_bytes = tpo_chamfer_loss_workspace_size(dt, B, N, M);
   auto ws = at::empty({(int64_t)ws_bytes}, xyz1.options().dtype(at::kByte));
   ok(tpo_chamfer_loss_fwd(dt, (int)flags, xyz1.data_ptr(), xyz2.data_ptr(), B, N, M, (int)reduction,
-                          loss.data_ptr(), idx1.data_ptr<int32_t>(), idx2.data_ptr<int32_t>(),
-                          ws.data_ptr(), ws_bytes, stream_of(xyz1)),
+                          loss.data_ptr(), ws.data_ptr(), ws_bytes, stream_of(xyz1)),
      "chamfer_loss");
-  return {loss, idx1, idx2};
+  return {loss, ws};
 }
 
 std::tuple<at::Tensor, at::Tensor> chamfer_loss_backward(const at::Tensor& xyz1_,
                                                          const at::Tensor& xyz2_,
-                                                         const at::Tensor& idx1,
-                                                         const at::Tensor& idx2,
+                                                         const at::Tensor& state,
                                                          const at::Tensor& grad_loss,
-                                                         int64_t reduction) {
+                                                         int64_t reduction, int64_t flags) {
   const c10::cuda::CUDAGuard g(xyz1_.device());
   const at::Tensor xyz1 = xyz1_.contiguous(), xyz2 = xyz2_.contiguous();
   const int64_t B = xyz1.size(0), N = xyz1.size(1), M = xyz2.size(1);
+  const int dt = to_dtype(xyz1);
+  TORCH_CHECK(state.numel() >= (int64_t)tpo_chamfer_loss_workspace_size(dt, B, N, M),
+              "chamfer_loss_backward: state does not belong to these inputs");
   const at::Tensor gl = grad_loss.to(xyz1.scalar_type()).reshape({1}).contiguous();
   auto gx1 = at::empty_like(xyz1);
   auto gx2 = at::empty_like(xyz2);
-  ok(tpo_chamfer_loss_bwd(to_dtype(xyz1), xyz1.data_ptr(), xyz2.data_ptr(), B, N, M, (int)reduction,
-                          idx1.data_ptr<int32_t>(), idx2.data_ptr<int32_t>(), gl.data_ptr(),
-                          gx1.data_ptr(), gx2.data_ptr(), stream_of(xyz1)),
+  ok(tpo_chamfer_loss_bwd(dt, (int)flags, xyz1.data_ptr(), xyz2.data_ptr(), B, N, M, (int)reduction,
+                          state.data_ptr(), gl.data_ptr(), gx1.data_ptr(), gx2.data_ptr(),
+                          stream_of(xyz1)),
      "chamfer_loss_backward");
   return {gx1, gx2};
 }
@@ -298,9 +297,9 @@ TORCH_LIBRARY(torch_point_ops_b200_chamfer, m) {
   m.def("chamfer_backward(Tensor xyz1, Tensor xyz2, Tensor idx1, Tensor idx2, "
         "Tensor grad_dist1, Tensor grad_dist2) -> (Tensor, Tensor)");
   m.def("chamfer_forward_ex(Tensor xyz1, Tensor xyz2, int flags) -> (Tensor, Tensor, Tensor, Tensor)");
-  m.def("chamfer_loss(Tensor xyz1, Tensor xyz2, int reduction, int flags) -> (Tensor, Tensor, Tensor)");
-  m.def("chamfer_loss_backward(Tensor xyz1, Tensor xyz2, Tensor idx1, Tensor idx2, "
-        "Tensor grad_loss, int reduction) -> (Tensor, Tensor)");
+  m.def("chamfer_loss(Tensor xyz1, Tensor xyz2, int reduction, int flags) -> (Tensor, Tensor)");
+  m.def("chamfer_loss_backward(Tensor xyz1, Tensor xyz2, Tensor state, Tensor grad_loss, "
+        "int reduction, int flags) -> (Tensor, Tensor)");
   m.def("chamfer_keys_empty(Tensor like, int n) -> Tensor");
   m.def("chamfer_fwd_keys(Tensor xyz1, Tensor xyz2, int row_begin, int row_end, int flags, "
         "Tensor(a!) keys1, Tensor(b!) keys2) -> ()");

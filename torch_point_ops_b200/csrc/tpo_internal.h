@@ -45,6 +45,17 @@ int knn_gather_backward(int dtype, const void* gout, const int64_t* idx, const i
                         int64_t N, int64_t M, int64_t U, int64_t L, int64_t K, void* gx,
                         cudaStream_t st);
 
+// Fused-loss forward on the fp32 keys kernel (rows 0..N, all columns).  lossws:
+// keys_loss_bytes(B) bytes whose first keys_loss_counter_bytes(B) are 0xff-filled.
+inline size_t keys_loss_counter_bytes(int64_t B) { return ((size_t)(B + 1) * 4 + 255) & ~(size_t)255; }
+inline size_t keys_loss_bytes(int64_t B) { return keys_loss_counter_bytes(B) + (((size_t)B * 16 + 255) & ~(size_t)255); }
+int chamfer_loss_keys_f32(int flags, const void* x1, const void* x2, int64_t B, int64_t N,
+                          int64_t M, int reduction, void* k1, void* k2, void* lossws, void* loss,
+                          cudaStream_t st);
+int chamfer_bwd_from_keys_f32(int flags, const void* x1, const void* x2, int64_t B, int64_t N,
+                              int64_t M, const void* k1, const void* k2, const void* grad_loss,
+                              int reduction, void* gx1, void* gx2, cudaStream_t st);
+
 inline int dtype_size(int dtype) {
   return dtype == TPO_F32 ? 4 : dtype == TPO_F16 ? 2 : dtype == TPO_F64 ? 8 : 0;
 }
