@@ -486,6 +486,67 @@ def cpu_measure(cfg, host_inputs, budget_s=15.0):
             "sample": sample, "seconds": round(dt, 3)}
 
 
+def run_reference_cuda(args, cfg):
+    """Context only (not the driver's reference arm): the reference's own CUDA
+    kernels, compiled unmodified from its sources into oracle/_ref, timed on this
+    GPU for the same step (chamfer_forward, the two torch means, chamfer_backward;
+    knn_forward + python sort + gather, knn_backward).  Eager: the reference
+    launches on the legacy default stream, which cannot be graph-captured."""
+    import oracle
+
+    ws, rank, local = dist_env()
+    if rank != 0:
+        return None
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    host_inputs = make_inputs(cfg, seed=1000)
+    pairs = pairs_of(cfg, host_inputs)
+    x = [t.to(dev) for t in host_inputs]
+    if cfg["kind"] == "chamfer":
+        ops = oracle.ref_chamfer()
+        if ops is None:
+            return {"impl": "reference_cuda", "unavailable": "oracle/_ref/chamfer_cuda_ref.so not built"}
+        B, N, M = cfg["B"], cfg["N"], cfg["M"]
+
+        def step():
+            d1, d2, i1, i2 = ops.chamfer_forward(x[0], x[1])
+            loss = d1.mean() + d2.mean()
+            g1 = torch.full_like(d1, 1.0 / (B * N))
+            g2 = torch.full_like(d2, 1.0 / (B * M))
+            return loss, ops.chamfer_backward(x[0], x[1], i1, i2, g1, g2)
+    else:
+        ops = oracle.ref_knn()
+        if ops is None or not oracle._ref_loaded.get("knn_cuda_ref.so"):
+            return {"impl": "reference_cuda", "unavailable": "oracle/_ref/knn_cuda_ref.so not built"}
+        p1, p2, l1, l2 = x
+        K = cfg["K"]
+
+        def step():
+            idx, d = ops.knn_forward(p1, p2, l1, l2, 2, K, -1)
+            d, o = d.sort(dim=2)
+            idx = idx.gather(2, o)
+            nn = p2[:, :, None].expand(-1, -1, K, -1).gather(1, idx[..., None].expand(-1, -1, -1, 3))
+            g = torch.ones_like(d)
+            return nn.sum(), ops.knn_backward(p1, p2, l1, l2, idx, 2, g)
+    flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    tot = 0.0
+    for i in range(args.steps):
+        flush.fill_(float(i))
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        step()
+        b.record()
+        b.synchronize()
+        tot += a.elapsed_time(b)
+    ms = tot / args.steps
+    return {"impl": "reference_cuda", "metric": "reference CUDA kernels, same step (context)",
+            "value": round(pairs / (ms * 1e-3) / 1e9, 2), "unit": "Gpair/s",
+            "ms_per_step": round(ms, 4), "config": {"workload": cfg["desc"]}}
+
+
 def run_reference(args, cfg):
     """Reference arm: the reference's own CPU implementation of the path on this
     host's cores (the reference chamfer has no CPU kernel; its CPU path is knn K=1
@@ -523,13 +584,18 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="2", choices=sorted(CONFIGS))
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference_cuda"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     cfg = CONFIGS[args.config]
     ws, rank, _ = dist_env()
 
+    if args.impl == "reference_cuda":
+        line = run_reference_cuda(args, cfg)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
     if args.impl == "reference":
         line = run_reference(args, cfg)
         if line is not None:

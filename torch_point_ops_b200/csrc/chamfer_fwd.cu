@@ -93,10 +93,10 @@ __device__ __forceinline__ void block_sum2(double& a, double& c, double* sa, dou
   for (int w = 0; w < (int)(blockDim.x >> 5); ++w) { a += sa[w]; c += sc[w]; }
 }
 
-// Sum of the distances held in n keys by this block, in a fixed order: 8
+// Sum of the distances held in n keys by this block, in a fixed order: 32
 // independent loads in flight per thread (the loads, not the adds, set the time).
 __device__ __forceinline__ double sum_key_values(const u64* k, int64_t n) {
-  constexpr int U = 8;
+  constexpr int U = 32;
   double acc[U];
 #pragma unroll
   for (int u = 0; u < U; ++u) acc[u] = 0.0;
@@ -137,13 +137,15 @@ __device__ void keys_loss_epilogue(const KeysLoss& kl, const u64* keys1, const u
     s_glob = atomicAdd(kl.glob_ctr, 1u) == (unsigned)(B - 2);
   }
   __syncthreads();
-  if (!s_glob || threadIdx.x != 0) return;
+  if (!s_glob) return;
   __threadfence();
   double ta = 0.0, tc = 0.0;
-  for (int64_t k = 0; k < B; ++k) {
+  for (int64_t k = threadIdx.x; k < B; k += blockDim.x) {
     ta += __ldcg(kl.batch_part + 2 * k);
     tc += __ldcg(kl.batch_part + 2 * k + 1);
   }
+  block_sum2(ta, tc, sa, sc);
+  if (threadIdx.x != 0) return;
   // torch semantics: each mean (or sum) rounded to float, then added in float
   const float t1 = kl.reduction == 0 ? (float)(ta / (double)(B * N)) : (float)ta;
   const float t2 = kl.reduction == 0 ? (float)(tc / (double)(B * M)) : (float)tc;
