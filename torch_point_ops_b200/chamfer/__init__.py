@@ -54,25 +54,7 @@ def _(xyz1, xyz2, idx1, idx2, grad_dist1, grad_dist2):
     return torch.empty_like(xyz1), torch.empty_like(xyz2)
 
 
-def _loss_setup(ctx, inputs, output):
-    xyz1, xyz2, reduction, flags = inputs
-    _, state = output
-    ctx.save_for_backward(xyz1, xyz2, state)
-    ctx.reduction = reduction
-    ctx.flags = flags
-    ctx.set_materialize_grads(False)
-
-
-def _loss_backward(ctx, grad_loss, grad_state):
-    xyz1, xyz2, state = ctx.saved_tensors
-    if grad_loss is None:
-        return None, None, None, None
-    gx1, gx2 = _ops.chamfer_loss_backward(xyz1, xyz2, state, grad_loss, ctx.reduction, ctx.flags)
-    return gx1, gx2, None, None
-
-
-torch.library.register_autograd(
-    "torch_point_ops_b200_chamfer::chamfer_loss", _loss_backward, setup_context=_loss_setup)
+# chamfer_loss has its autograd formula registered in C++ (csrc/torch_ops.cpp).
 
 
 @torch.library.register_fake("torch_point_ops_b200_chamfer::chamfer_loss")

@@ -13,6 +13,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/library.h>
 #include <torch/all.h>
+#include <torch/autograd.h>
 
 #include "../../include/tpo_b200.h"
 
@@ -134,6 +135,38 @@ std::tuple<at::Tensor, at::Tensor> chamfer_loss_backward(const at::Tensor& xyz1_
                           stream_of(xyz1)),
      "chamfer_loss_backward");
   return {gx1, gx2};
+}
+
+// Autograd for the fused loss in C++ (no Python on the training-step path).
+class ChamferLossFn : public torch::autograd::Function<ChamferLossFn> {
+ public:
+  static torch::autograd::variable_list forward(torch::autograd::AutogradContext* ctx,
+                                                const at::Tensor& xyz1, const at::Tensor& xyz2,
+                                                int64_t reduction, int64_t flags) {
+    at::AutoDispatchBelowADInplaceOrView guard;
+    auto out = chamfer_loss(xyz1, xyz2, reduction, flags);
+    ctx->save_for_backward({xyz1, xyz2, std::get<1>(out)});
+    ctx->saved_data["reduction"] = reduction;
+    ctx->saved_data["flags"] = flags;
+    ctx->mark_non_differentiable({std::get<1>(out)});
+    return {std::get<0>(out), std::get<1>(out)};
+  }
+  static torch::autograd::variable_list backward(torch::autograd::AutogradContext* ctx,
+                                                 torch::autograd::variable_list grads) {
+    auto saved = ctx->get_saved_variables();
+    if (!grads[0].defined()) return {at::Tensor(), at::Tensor(), at::Tensor(), at::Tensor()};
+    auto g = chamfer_loss_backward(saved[0], saved[1], saved[2], grads[0],
+                                   ctx->saved_data["reduction"].toInt(),
+                                   ctx->saved_data["flags"].toInt());
+    return {std::get<0>(g), std::get<1>(g), at::Tensor(), at::Tensor()};
+  }
+};
+
+std::tuple<at::Tensor, at::Tensor> chamfer_loss_autograd(const at::Tensor& xyz1,
+                                                         const at::Tensor& xyz2,
+                                                         int64_t reduction, int64_t flags) {
+  auto r = ChamferLossFn::apply(xyz1, xyz2, reduction, flags);
+  return {r[0], r[1]};
 }
 
 // ---- row-sharded split (multi-GPU): keys live in int64 tensors ----
@@ -320,6 +353,10 @@ TORCH_LIBRARY_IMPL(torch_point_ops_b200_chamfer, CUDA, m) {
   m.impl("chamfer_fwd_keys", &chamfer_fwd_keys);
   m.impl("chamfer_finalize", &chamfer_finalize);
   m.impl("chamfer_bwd_partial", &chamfer_bwd_partial);
+}
+
+TORCH_LIBRARY_IMPL(torch_point_ops_b200_chamfer, Autograd, m) {
+  m.impl("chamfer_loss", &chamfer_loss_autograd);
 }
 
 TORCH_LIBRARY(torch_point_ops_b200_knn, m) {
