@@ -184,9 +184,26 @@ __global__ void __launch_bounds__(CF_MAXW * 32, TPO_CF_MINB)
   {
     const int64_t nrow = min64((int64_t)W * CF_ROWS_PER_WARP, max64(row_end - blk_row0, 0));
     const float* src = xyz1 + (b * N + blk_row0) * 3;
+#pragma unroll 8
     for (int e = threadIdx.x; e < W * CF_ROWS_PER_WARP * 3; e += blockDim.x)
       s_rows[e] = e < nrow * 3 ? __ldg(src + e) : qnan;
   }
+  // a column tile: xyz2[tc, tc+256) of this batch, duplicated {c,c}, NaN-padded to
+  // a whole number of 8-column chunks
+  auto stage_tile = [&](int64_t tc) {
+    const int ncols = (int)min64(CF_TILE, c1 - tc);
+    const int nsteps = ((ncols + CF_CHUNK - 1) / CF_CHUNK) * 2;
+    const float* src = xyz2 + (b * M + tc) * 3;
+    float2* dst = &s_col[0][0][0];
+#pragma unroll 4
+    for (int e = threadIdx.x; e < nsteps * CF_C * 3; e += blockDim.x) {
+      const int col = e / 3;
+      const int comp = e - col * 3;
+      const float v = col < ncols ? __ldg(src + e) : qnan;
+      dst[((col >> 2) * 3 + comp) * CF_C + (col & 3)] = make_float2(v, v);
+    }
+  };
+  if (c0 < c1) stage_tile(c0);
   __syncthreads();
   u64 QX[CF_RP], QY[CF_RP], QZ[CF_RP];
   {
@@ -209,19 +226,11 @@ __global__ void __launch_bounds__(CF_MAXW * 32, TPO_CF_MINB)
   for (int64_t tc = c0; tc < c1; tc += CF_TILE) {
     const int ncols = (int)min64(CF_TILE, c1 - tc);
     const int nsteps = ((ncols + CF_CHUNK - 1) / CF_CHUNK) * 2;  // even: 8-column chunks
-    __syncthreads();
-    {
-      const float* src = xyz2 + (b * M + tc) * 3;
-      float* dst = reinterpret_cast<float*>(&s_col[0][0][0]);
-      for (int e = threadIdx.x; e < nsteps * CF_C * 3; e += blockDim.x) {
-        const int col = e / 3;
-        const int comp = e - col * 3;
-        const float v = col < ncols ? __ldg(src + e) : qnan;
-        const int o = ((col >> 2) * 3 + comp) * CF_C + (col & 3);
-        reinterpret_cast<float2*>(dst)[o] = make_float2(v, v);
-      }
+    if (tc != c0) {  // the first tile was staged together with the rows
+      __syncthreads();
+      stage_tile(tc);
+      __syncthreads();
     }
-    __syncthreads();
     if (warp_active) {
       // Two 4-column sub-steps per iteration; the row-side chunk is 8 columns.
 #pragma unroll 1
