@@ -117,28 +117,33 @@ __device__ __forceinline__ double sum_key_values(const u64* k, int64_t n) {
   return t;
 }
 
+__device__ __forceinline__ unsigned atom_add_acq_rel(unsigned* p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
 __device__ void keys_loss_epilogue(const KeysLoss& kl, const u64* keys1, const u64* keys2,
                                    int64_t b, int64_t B, int64_t N, int64_t M, int per_batch) {
   __shared__ double sa[CF_MAXW], sc[CF_MAXW];
   __shared__ bool s_last;
-  __threadfence();  // this thread's key reductions before the counter
+  // The barrier orders every thread's key reductions before thread 0's
+  // acq_rel counter update (release is cumulative); the last CTA's acquire,
+  // carried to its other threads by the next barrier, makes all CTAs' keys visible.
   __syncthreads();
-  if (threadIdx.x == 0) s_last = atomicAdd(kl.batch_ctr + b, 1u) == (unsigned)(per_batch - 2);
+  if (threadIdx.x == 0) s_last = atom_add_acq_rel(kl.batch_ctr + b, 1u) == (unsigned)(per_batch - 2);
   __syncthreads();
   if (!s_last) return;
-  __threadfence();
   double a = sum_key_values(keys1 + b * N, N), c = sum_key_values(keys2 + b * M, M);
   block_sum2(a, c, sa, sc);
   __shared__ bool s_glob;
   if (threadIdx.x == 0) {
     __stcg(kl.batch_part + 2 * b, a);
     __stcg(kl.batch_part + 2 * b + 1, c);
-    __threadfence();
-    s_glob = atomicAdd(kl.glob_ctr, 1u) == (unsigned)(B - 2);
+    s_glob = atom_add_acq_rel(kl.glob_ctr, 1u) == (unsigned)(B - 2);
   }
   __syncthreads();
   if (!s_glob) return;
-  __threadfence();
   double ta = 0.0, tc = 0.0;
   for (int64_t k = threadIdx.x; k < B; k += blockDim.x) {
     ta += __ldcg(kl.batch_part + 2 * k);
