@@ -182,7 +182,7 @@ static LossLayout loss_layout(int dtype, int64_t B, int64_t N, int64_t M) {
   return L;
 }
 static bool loss_uses_keys_kernel(int dtype, int64_t B, int64_t N, int64_t M) {
-  return dtype == TPO_F32 && B > 0 && N > 0 && M > 0;
+  return (dtype == TPO_F32 || dtype == TPO_F16) && B > 0 && N > 0 && M > 0;
 }
 
 size_t tpo_chamfer_loss_workspace_size(int dtype, int64_t B, int64_t N, int64_t M) {
@@ -209,7 +209,7 @@ int tpo_chamfer_loss_fwd(int dtype, int flags, const void* xyz1, const void* xyz
   if (loss_uses_keys_kernel(dtype, B, N, M)) {
     // keys to the empty key and the reduction counters to 0xffffffff: one fill
     if ((s = cuda_status(cudaMemsetAsync(w, 0xff, L.kl + keys_loss_counter_bytes(B), st)))) return s;
-    return chamfer_loss_keys_f32(flags, xyz1, xyz2, B, N, M, reduction, k1, k2, w + L.kl, loss, st);
+    return chamfer_loss_keys(dtype, flags, xyz1, xyz2, B, N, M, reduction, k1, k2, w + L.kl, loss, st);
   }
   if (L.kl && (s = cuda_status(cudaMemsetAsync(w, 0xff, L.kl, st)))) return s;
   if ((s = cuda_status(cudaMemsetAsync(w + L.fin + kFinPartialBytes, 0xff, 256, st)))) return s;
@@ -238,7 +238,7 @@ int tpo_chamfer_loss_bwd(int dtype, int flags, const void* xyz1, const void* xyz
   const char* w = (const char*)workspace;
   if (loss_uses_keys_kernel(dtype, B, N, M)) {
     const size_t kb = (size_t)tpo_chamfer_key_bytes(dtype);
-    return chamfer_bwd_from_keys_f32(flags, xyz1, xyz2, B, N, M, w,
+    return chamfer_bwd_from_keys(dtype, flags, xyz1, xyz2, B, N, M, w,
                                      w + align256(kb * (size_t)B * (size_t)N), grad_loss,
                                      reduction, grad_xyz1, grad_xyz2, st);
   }

@@ -44,7 +44,10 @@ constexpr int CF_C = 4;               // columns per sub-step
 constexpr int CF_CHUNK = 2 * CF_C;    // row-side chunk (columns per key)
 constexpr int CF_TILE_STEPS = 64;     // steps per shared-memory tile
 constexpr int CF_TILE = CF_TILE_STEPS * CF_C;
-constexpr int CF_MAXW = 4;            // warps per CTA
+#ifndef TPO_CF_MAXW
+#define TPO_CF_MAXW 4
+#endif
+constexpr int CF_MAXW = TPO_CF_MAXW;  // warps per CTA
 constexpr int CF_ROWS_PER_WARP = 32 * CF_R;
 
 // min over R values with 3-input FMNMX, as a balanced tree
@@ -74,8 +77,9 @@ struct KeysLoss {
   unsigned* batch_ctr;  // [B]
   unsigned* glob_ctr;   // [1]
   double* batch_part;   // [2B]
-  float* loss;          // nullptr: no fused loss
+  void* loss;           // nullptr: no fused loss
   int reduction;        // 0 mean(d1)+mean(d2), 1 sum(d1)+sum(d2)
+  int half_out;         // loss is fp16 (else fp32)
 };
 
 __device__ __forceinline__ void block_sum2(double& a, double& c, double* sa, double* sc) {
@@ -152,9 +156,12 @@ __device__ void keys_loss_epilogue(const KeysLoss& kl, const u64* keys1, const u
   block_sum2(ta, tc, sa, sc);
   if (threadIdx.x != 0) return;
   // torch semantics: each mean (or sum) rounded to float, then added in float
-  const float t1 = kl.reduction == 0 ? (float)(ta / (double)(B * N)) : (float)ta;
-  const float t2 = kl.reduction == 0 ? (float)(tc / (double)(B * M)) : (float)tc;
-  *kl.loss = __fadd_rn(t1, t2);
+  const double v1 = kl.reduction == 0 ? ta / (double)(B * N) : ta;
+  const double v2 = kl.reduction == 0 ? tc / (double)(B * M) : tc;
+  if (kl.half_out)  // c10::Half: each term rounded to half, added with half rounding
+    *(__half*)kl.loss = hadd_rn(__float2half_rn((float)v1), __float2half_rn((float)v2));
+  else
+    *(float*)kl.loss = __fadd_rn((float)v1, (float)v2);
 }
 
 template <int MODE>
@@ -314,6 +321,180 @@ __global__ void __launch_bounds__(CF_MAXW * 32, TPO_CF_MINB)
       if (row < row_end)
         red_min_u64(keys1 + b * N + row,
                     ((u64)__float_as_uint(best[r]) << 32) | (unsigned)bchunk[r]);
+    }
+  }
+  if (kl.loss != nullptr)
+    keys_loss_epilogue(kl, keys1, keys2, b, (int64_t)gridDim.x / (rb_count * cs_count), N, M,
+                       rb_count * cs_count);
+}
+
+// ----------------------------- fp16 fast path -----------------------------
+// The fp32 kernel's structure on packed f16x2: a register holds the same
+// coordinate of two rows, shared memory holds {c,c} per column, and every
+// sub/mul/add rounds to half (c10::Half semantics, chamfer.cu:64-67).  Row minima
+// are packed f16x2 mins; column minima reduce the half bit patterns (ordered
+// like the values for d >= 0) with redux.sync.  Keys store the distance as the
+// bits of its exact float value, like the generic path, so finalize is shared.
+__device__ __forceinline__ unsigned short h_lo(h2 v) { return (unsigned short)(v & 0xffffu); }
+__device__ __forceinline__ unsigned short h_hi(h2 v) { return (unsigned short)(v >> 16); }
+__device__ __forceinline__ unsigned hbits_to_fbits(unsigned hb) {
+  return __float_as_uint(__half2float(__ushort_as_half((unsigned short)hb)));
+}
+
+__global__ void __launch_bounds__(CF_MAXW * 32, TPO_CF_MINB)
+    chamfer_keys_f16_kernel(const __half* __restrict__ xyz1, const __half* __restrict__ xyz2,
+                            int64_t N, int64_t M, int64_t row_begin, int64_t row_end,
+                            int rb_count, int cs_count, int64_t seg,
+                            u64* __restrict__ keys1, u64* __restrict__ keys2, KeysLoss kl) {
+  __shared__ __align__(16) h2 s_col[CF_TILE_STEPS][3][CF_C];
+  __shared__ __align__(16) uint2 s_wb[CF_MAXW][CF_TILE];  // {ballot, half distance bits}
+  __shared__ __align__(16) __half s_rows[CF_MAXW * CF_ROWS_PER_WARP * 3];
+
+  const int W = blockDim.x >> 5;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  int64_t unit = blockIdx.x;
+  const int cs = (int)(unit % cs_count);
+  unit /= cs_count;
+  const int rb = (int)(unit % rb_count);
+  const int64_t b = unit / rb_count;
+  const int64_t c0 = (int64_t)cs * seg;
+  const int64_t c1 = min(M, c0 + seg);
+  const int64_t blk_row0 = row_begin + (int64_t)rb * W * CF_ROWS_PER_WARP;
+  const int64_t warp_row0 = blk_row0 + (int64_t)warp * CF_ROWS_PER_WARP;
+  const int64_t lane_row0 = warp_row0 + (int64_t)lane * CF_R;
+  const bool warp_active = warp_row0 < row_end;
+  const int n_active = (int)min64(W, (row_end - blk_row0 + CF_ROWS_PER_WARP - 1) / CF_ROWS_PER_WARP);
+  const unsigned short hnan = 0x7fff;
+
+  {
+    const int64_t nrow = min64((int64_t)W * CF_ROWS_PER_WARP, max64(row_end - blk_row0, 0));
+    const __half* src = xyz1 + (b * N + blk_row0) * 3;
+#pragma unroll 8
+    for (int e = threadIdx.x; e < W * CF_ROWS_PER_WARP * 3; e += blockDim.x)
+      s_rows[e] = e < nrow * 3 ? src[e] : __ushort_as_half(hnan);
+  }
+  auto stage_tile = [&](int64_t tc) {
+    const int ncols = (int)min64(CF_TILE, c1 - tc);
+    const int nsteps = ((ncols + CF_CHUNK - 1) / CF_CHUNK) * 2;
+    const unsigned short* src = reinterpret_cast<const unsigned short*>(xyz2 + (b * M + tc) * 3);
+    h2* dst = &s_col[0][0][0];
+#pragma unroll 4
+    for (int e = threadIdx.x; e < nsteps * CF_C * 3; e += blockDim.x) {
+      const int col = e / 3;
+      const int comp = e - col * 3;
+      const unsigned short v = col < ncols ? src[e] : hnan;
+      dst[((col >> 2) * 3 + comp) * CF_C + (col & 3)] = hpk(v, v);
+    }
+  };
+  if (c0 < c1) stage_tile(c0);
+  __syncthreads();
+  h2 QX[CF_RP], QY[CF_RP], QZ[CF_RP];
+  {
+    const unsigned short* a = reinterpret_cast<const unsigned short*>(s_rows) +
+                              (warp * CF_ROWS_PER_WARP + lane * CF_R) * 3;
+#pragma unroll
+    for (int p = 0; p < CF_RP; ++p) {
+      QX[p] = hpk(a[6 * p + 0], a[6 * p + 3]);
+      QY[p] = hpk(a[6 * p + 1], a[6 * p + 4]);
+      QZ[p] = hpk(a[6 * p + 2], a[6 * p + 5]);
+    }
+  }
+  h2 best[CF_RP];
+  int bchunk[CF_R];
+#pragma unroll
+  for (int p = 0; p < CF_RP; ++p) best[p] = hpk(0x7c00, 0x7c00);  // +inf, +inf
+#pragma unroll
+  for (int r = 0; r < CF_R; ++r) bchunk[r] = 0;
+
+  for (int64_t tc = c0; tc < c1; tc += CF_TILE) {
+    const int ncols = (int)min64(CF_TILE, c1 - tc);
+    const int nsteps = ((ncols + CF_CHUNK - 1) / CF_CHUNK) * 2;
+    if (tc != c0) {
+      __syncthreads();
+      stage_tile(tc);
+      __syncthreads();
+    }
+    if (warp_active) {
+#pragma unroll 1
+      for (int s = 0; s < nsteps; s += 2) {
+        h2 rm[CF_RP];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint4 xa = *reinterpret_cast<const uint4*>(&s_col[s + h][0][0]);
+          const uint4 ya = *reinterpret_cast<const uint4*>(&s_col[s + h][1][0]);
+          const uint4 za = *reinterpret_cast<const uint4*>(&s_col[s + h][2][0]);
+          const h2 X[CF_C] = {xa.x, xa.y, xa.z, xa.w};
+          const h2 Y[CF_C] = {ya.x, ya.y, ya.z, ya.w};
+          const h2 Z[CF_C] = {za.x, za.y, za.z, za.w};
+          h2 d[CF_C][CF_RP];
+#pragma unroll
+          for (int c = 0; c < CF_C; ++c)
+#pragma unroll
+            for (int p = 0; p < CF_RP; ++p)
+              d[c][p] = hdist2(hsub2r(X[c], QX[p]), hsub2r(Y[c], QY[p]), hsub2r(Z[c], QZ[p]));
+#pragma unroll
+          for (int p = 0; p < CF_RP; ++p) {
+            const h2 m = hmin2r(h == 0 ? best[p] : rm[p], hmin2r(d[0][p], d[1][p]));
+            rm[p] = hmin2r(m, hmin2r(d[2][p], d[3][p]));
+          }
+#pragma unroll
+          for (int c = 0; c < CF_C; ++c) {
+            h2 m = d[c][0];
+#pragma unroll
+            for (int p = 1; p < CF_RP; ++p) m = hmin2r(m, d[c][p]);
+            const h2 mm = hmin2r(m, m >> 16);  // low half: min of both halves
+            const unsigned u = mm & 0xffffu;
+            const unsigned w = redux_min_u32(u);
+            const unsigned bal = __ballot_sync(0xffffffffu, u == w);
+            if (lane == 0) s_wb[warp][(s + h) * CF_C + c] = make_uint2(bal, w);
+          }
+        }
+        const int colbase = (int)(tc + s * CF_C);
+#pragma unroll
+        for (int p = 0; p < CF_RP; ++p) {
+          const unsigned lt = __hlt2_mask(*reinterpret_cast<const __half2*>(&rm[p]),
+                                          *reinterpret_cast<const __half2*>(&best[p]));
+          if (lt & 0xffffu) bchunk[2 * p] = colbase;
+          if (lt >> 16) bchunk[2 * p + 1] = colbase;
+          best[p] = rm[p];
+        }
+      }
+    }
+    __syncthreads();
+    for (int col = threadIdx.x; col < ncols; col += blockDim.x) {
+      unsigned bw = s_wb[0][col].y;
+      int wb = 0;
+      for (int w = 1; w < n_active; ++w) {
+        const unsigned v = s_wb[w][col].y;
+        if (v < bw) { bw = v; wb = w; }
+      }
+      const int lr0 = wb * CF_ROWS_PER_WARP + (__ffs(s_wb[wb][col].x) - 1) * CF_R;
+      const __half cx = __ushort_as_half(h_lo(s_col[col >> 2][0][col & 3]));
+      const __half cy = __ushort_as_half(h_lo(s_col[col >> 2][1][col & 3]));
+      const __half cz = __ushort_as_half(h_lo(s_col[col >> 2][2][col & 3]));
+      int found = 0;
+#pragma unroll
+      for (int k = CF_R - 1; k >= 0; --k) {
+        const __half* r = s_rows + (lr0 + k) * 3;
+        const __half dd = dist1h(hsub_rn(cx, r[0]), hsub_rn(cy, r[1]), hsub_rn(cz, r[2]));
+        if ((unsigned)__half_as_ushort(dd) == bw) found = k;
+      }
+      const u64 k = ((u64)hbits_to_fbits(bw) << 32) | (unsigned)(blk_row0 + lr0 + found);
+      red_min_u64(keys2 + b * M + tc + col, k);
+    }
+  }
+  if (warp_active) {
+#pragma unroll
+    for (int p = 0; p < CF_RP; ++p) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int r = 2 * p + h;
+        const int64_t row = lane_row0 + r;
+        const unsigned hb = h ? h_hi(best[p]) : h_lo(best[p]);
+        if (row < row_end)
+          red_min_u64(keys1 + b * N + row, ((u64)hbits_to_fbits(hb) << 32) | (unsigned)bchunk[r]);
+      }
     }
   }
   if (kl.loss != nullptr)
@@ -710,22 +891,44 @@ __global__ void chamfer_finalize_kernel(const T* __restrict__ xyz1, const T* __r
   *fl.loss = FinRound<T>::add(t1, t2);
 }
 
-// Backward of the fused loss straight from the forward's keys (fp32): each point
-// resolves its neighbour by rescanning its key's chunk (as the finalize kernel
-// does), then scatters (2g)(p - q) like chamfer_bwd_kernel, with g the loss
-// gradient scaled as torch's MeanBackward does (g / count) or unscaled (sum).
-template <int MODE>
-__global__ void chamfer_bwd_from_keys_f32_kernel(const float* __restrict__ xyz1,
-                                                 const float* __restrict__ xyz2, int64_t B,
-                                                 int64_t N, int64_t M,
-                                                 const u64* __restrict__ keys1,
-                                                 const u64* __restrict__ keys2,
-                                                 const float* __restrict__ grad_loss,
-                                                 int reduction, float* __restrict__ gx1,
-                                                 float* __restrict__ gx2) {
-  const float g = *grad_loss;
-  const float g1 = __fmul_rn(reduction == 0 ? __fdiv_rn(g, (float)(B * N)) : g, 2.0f);
-  const float g2 = __fmul_rn(reduction == 0 ? __fdiv_rn(g, (float)(B * M)) : g, 2.0f);
+// Backward of the fused loss straight from the forward's keys (fp32 / fp16):
+// each point takes its neighbour from its key (column keys hold the exact row;
+// row keys the first column of an 8-column chunk, rescanned as in finalize),
+// then scatters (2g)(p - q) like chamfer_bwd_kernel, with g the loss gradient
+// scaled as torch's MeanBackward does (g / count) or unscaled (sum).
+template <typename T>
+struct FkOps;
+template <>
+struct FkOps<float> {
+  __device__ static float scale(float g, int64_t n, int red) {
+    return __fmul_rn(red == 0 ? __fdiv_rn(g, (float)n) : g, 2.0f);
+  }
+  __device__ static float term(float g, float a, float b) { return __fmul_rn(g, __fsub_rn(a, b)); }
+  __device__ static void add(float* p, float v) { atomicAdd(p, v); }
+  __device__ static float neg(float v) { return -v; }
+};
+template <>
+struct FkOps<__half> {
+  __device__ static __half scale(__half g, int64_t n, int red) {
+    const __half gs = red == 0 ? __float2half_rn(__half2float(g) / (float)n) : g;
+    return hmul_rn(gs, __float2half_rn(2.0f));
+  }
+  __device__ static __half term(__half g, __half a, __half b) { return hmul_rn(g, hsub_rn(a, b)); }
+  __device__ static void add(__half* p, __half v) { atomicAdd(p, v); }
+  __device__ static __half neg(__half v) { return __hneg(v); }
+};
+
+template <typename T, int MODE>
+__global__ void chamfer_bwd_from_keys_kernel(const T* __restrict__ xyz1, const T* __restrict__ xyz2,
+                                             int64_t B, int64_t N, int64_t M,
+                                             const u64* __restrict__ keys1,
+                                             const u64* __restrict__ keys2,
+                                             const T* __restrict__ grad_loss, int reduction,
+                                             T* __restrict__ gx1, T* __restrict__ gx2) {
+  using O = FkOps<T>;
+  const T g = *grad_loss;
+  const T g1 = O::scale(g, B * N, reduction);
+  const T g2 = O::scale(g, B * M, reduction);
   const int64_t n1 = B * N;
   const int64_t total = n1 + B * M;
   for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total;
@@ -736,23 +939,22 @@ __global__ void chamfer_bwd_from_keys_f32_kernel(const float* __restrict__ xyz1,
     const int64_t b = u / P;
     const u64 key = row ? __ldg(keys1 + u) : __ldg(keys2 + u);
     if (Q == 0 || key == ~0ull) continue;
-    const float* own = (row ? xyz1 : xyz2) + u * 3;
-    const float* other = (row ? xyz2 : xyz1) + b * Q * 3;
-    const float q[3] = {own[0], own[1], own[2]};
+    const T* own = (row ? xyz1 : xyz2) + u * 3;
+    const T* other = (row ? xyz2 : xyz1) + b * Q * 3;
+    const T q[3] = {own[0], own[1], own[2]};
     const int64_t base = (unsigned)key;
-    // column keys hold the exact row; row keys hold the first column of an 8-column chunk
-    const int32_t j = row ? find_in_chunk<float, MODE, CF_CHUNK, true>(q, other, base,
-                                                                       min64(Q, base + CF_CHUNK), key)
+    const int32_t j = row ? find_in_chunk<T, MODE, CF_CHUNK, true>(q, other, base,
+                                                                   min64(Q, base + CF_CHUNK), key)
                           : (int32_t)base;
-    const float gg = row ? g1 : g2;
-    float* ga = (row ? gx1 : gx2) + u * 3;
-    float* gb = (row ? gx2 : gx1) + (b * Q + j) * 3;
-    const float* pb = other + (int64_t)j * 3;
+    const T gg = row ? g1 : g2;
+    T* ga = (row ? gx1 : gx2) + u * 3;
+    T* gb = (row ? gx2 : gx1) + (b * Q + j) * 3;
+    const T* pb = other + (int64_t)j * 3;
 #pragma unroll
     for (int d = 0; d < 3; ++d) {
-      const float v = __fmul_rn(gg, __fsub_rn(q[d], pb[d]));
-      atomicAdd(ga + d, v);
-      atomicAdd(gb + d, -v);
+      const T v = O::term(gg, q[d], pb[d]);
+      O::add(ga + d, v);
+      O::add(gb + d, O::neg(v));
     }
   }
 }
@@ -810,8 +1012,24 @@ int slots_for(KernelT kernel, int threads) {
 template <int MODE>
 int launch_keys_f32(const float* x1, const float* x2, int64_t B, int64_t N, int64_t M,
                     int64_t rb0, int64_t rb1, void* k1, void* k2, cudaStream_t st,
-                    KeysLoss kl = KeysLoss{nullptr, nullptr, nullptr, nullptr, 0}) {
+                    KeysLoss kl = KeysLoss{nullptr, nullptr, nullptr, nullptr, 0, 0}) {
   auto kern = chamfer_keys_f32_kernel<MODE>;
+  static thread_local int slots_cache[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int& slots = slots_cache[dev & 63];
+  if (!slots) slots = slots_for(kern, CF_MAXW * 32);
+  const Plan p = make_plan(B, rb1 - rb0, M, CF_ROWS_PER_WARP, CF_MAXW, slots);
+  if (p.ctas <= 0) return TPO_OK;
+  kern<<<(unsigned)p.ctas, p.warps * 32, 0, st>>>(x1, x2, N, M, rb0, rb1, p.rb_count, p.cs_count,
+                                                   p.seg, (u64*)k1, (u64*)k2, kl);
+  return check_launch();
+}
+
+int launch_keys_f16(const __half* x1, const __half* x2, int64_t B, int64_t N, int64_t M,
+                    int64_t rb0, int64_t rb1, void* k1, void* k2, cudaStream_t st,
+                    KeysLoss kl = KeysLoss{nullptr, nullptr, nullptr, nullptr, 0, 0}) {
+  auto kern = chamfer_keys_f16_kernel;
   static thread_local int slots_cache[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -873,7 +1091,7 @@ int chamfer_fwd_keys(int dtype, int flags, const void* x1, const void* x2, int64
       return exact ? launch_keys_f32<TPO_ROUND_EXACT>((const float*)x1, (const float*)x2, B, N, M, rb0, rb1, k1, k2, st)
                    : launch_keys_f32<TPO_ROUND_FMA>((const float*)x1, (const float*)x2, B, N, M, rb0, rb1, k1, k2, st);
     case TPO_F16:
-      return launch_keys_generic<__half, TPO_ROUND_EXACT>((const __half*)x1, (const __half*)x2, B, N, M, rb0, rb1, k1, k2, st);
+      return launch_keys_f16((const __half*)x1, (const __half*)x2, B, N, M, rb0, rb1, k1, k2, st);
     case TPO_F64:
       return exact ? launch_keys_generic<double, TPO_ROUND_EXACT>((const double*)x1, (const double*)x2, B, N, M, rb0, rb1, k1, k2, st)
                    : launch_keys_generic<double, TPO_ROUND_FMA>((const double*)x1, (const double*)x2, B, N, M, rb0, rb1, k1, k2, st);
@@ -893,7 +1111,7 @@ int chamfer_finalize(int dtype, int flags, const void* x1, const void* x2, int64
     case TPO_F32:
       return exact ? TPO_FIN(float, TPO_ROUND_EXACT, CF_CHUNK, 1) : TPO_FIN(float, TPO_ROUND_FMA, CF_CHUNK, 1);
     case TPO_F16:
-      return TPO_FIN(__half, TPO_ROUND_EXACT, CG_C, CG_R);
+      return TPO_FIN(__half, TPO_ROUND_EXACT, CF_CHUNK, 1);
     case TPO_F64:
       return exact ? TPO_FIN(double, TPO_ROUND_EXACT, CG_C, CG_R) : TPO_FIN(double, TPO_ROUND_FMA, CG_C, CG_R);
   }
@@ -901,36 +1119,46 @@ int chamfer_finalize(int dtype, int flags, const void* x1, const void* x2, int64
   return TPO_ERR_INVALID_ARGUMENT;
 }
 
-int chamfer_loss_keys_f32(int flags, const void* x1, const void* x2, int64_t B, int64_t N,
-                          int64_t M, int reduction, void* k1, void* k2, void* lossws, void* loss,
-                          cudaStream_t st) {
+int chamfer_loss_keys(int dtype, int flags, const void* x1, const void* x2, int64_t B, int64_t N,
+                      int64_t M, int reduction, void* k1, void* k2, void* lossws, void* loss,
+                      cudaStream_t st) {
   KeysLoss kl;
   kl.batch_ctr = (unsigned*)lossws;
   kl.glob_ctr = kl.batch_ctr + B;
   kl.batch_part = (double*)((char*)lossws + keys_loss_counter_bytes(B));
-  kl.loss = (float*)loss;
+  kl.loss = loss;
+  kl.half_out = dtype == TPO_F16;
   kl.reduction = reduction;
+  if (dtype == TPO_F16)
+    return launch_keys_f16((const __half*)x1, (const __half*)x2, B, N, M, 0, N, k1, k2, st, kl);
   const bool exact = (flags & TPO_ROUND_EXACT) != 0;
   return exact ? launch_keys_f32<TPO_ROUND_EXACT>((const float*)x1, (const float*)x2, B, N, M, 0, N, k1, k2, st, kl)
                : launch_keys_f32<TPO_ROUND_FMA>((const float*)x1, (const float*)x2, B, N, M, 0, N, k1, k2, st, kl);
 }
 
-int chamfer_bwd_from_keys_f32(int flags, const void* x1, const void* x2, int64_t B, int64_t N,
-                              int64_t M, const void* k1, const void* k2, const void* grad_loss,
-                              int reduction, void* gx1, void* gx2, cudaStream_t st) {
+int chamfer_bwd_from_keys(int dtype, int flags, const void* x1, const void* x2, int64_t B,
+                          int64_t N, int64_t M, const void* k1, const void* k2,
+                          const void* grad_loss, int reduction, void* gx1, void* gx2,
+                          cudaStream_t st) {
   const int64_t total = B * (N + M);
   if (total <= 0) return TPO_OK;
   const int threads = 256;
   const unsigned blocks = (unsigned)std::min<int64_t>((total + threads - 1) / threads, 148 * 16);
   const bool exact = (flags & TPO_ROUND_EXACT) != 0;
-  if (exact)
-    chamfer_bwd_from_keys_f32_kernel<TPO_ROUND_EXACT><<<blocks, threads, 0, st>>>(
-        (const float*)x1, (const float*)x2, B, N, M, (const u64*)k1, (const u64*)k2,
-        (const float*)grad_loss, reduction, (float*)gx1, (float*)gx2);
+  const u64* K1 = (const u64*)k1;
+  const u64* K2 = (const u64*)k2;
+  if (dtype == TPO_F16)
+    chamfer_bwd_from_keys_kernel<__half, TPO_ROUND_EXACT><<<blocks, threads, 0, st>>>(
+        (const __half*)x1, (const __half*)x2, B, N, M, K1, K2, (const __half*)grad_loss,
+        reduction, (__half*)gx1, (__half*)gx2);
+  else if (exact)
+    chamfer_bwd_from_keys_kernel<float, TPO_ROUND_EXACT><<<blocks, threads, 0, st>>>(
+        (const float*)x1, (const float*)x2, B, N, M, K1, K2, (const float*)grad_loss, reduction,
+        (float*)gx1, (float*)gx2);
   else
-    chamfer_bwd_from_keys_f32_kernel<TPO_ROUND_FMA><<<blocks, threads, 0, st>>>(
-        (const float*)x1, (const float*)x2, B, N, M, (const u64*)k1, (const u64*)k2,
-        (const float*)grad_loss, reduction, (float*)gx1, (float*)gx2);
+    chamfer_bwd_from_keys_kernel<float, TPO_ROUND_FMA><<<blocks, threads, 0, st>>>(
+        (const float*)x1, (const float*)x2, B, N, M, K1, K2, (const float*)grad_loss, reduction,
+        (float*)gx1, (float*)gx2);
   return check_launch();
 }
 

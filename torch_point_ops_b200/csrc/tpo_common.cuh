@@ -115,6 +115,36 @@ __device__ __forceinline__ __half dist1h(__half dx, __half dy, __half dz) {
   return hadd_rn(hadd_rn(hmul_rn(dx, dx), hmul_rn(dy, dy)), hmul_rn(dz, dz));
 }
 
+// Packed f16x2 (two rows in one 32-bit register), every operation rounded (.rn).
+typedef unsigned h2;  // raw f16x2 bits
+__device__ __forceinline__ h2 hsub2r(h2 a, h2 b) {
+  h2 r;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ h2 hmul2r(h2 a, h2 b) {
+  h2 r;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ h2 hadd2r(h2 a, h2 b) {
+  h2 r;
+  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ h2 hmin2r(h2 a, h2 b) {
+  h2 r;
+  asm("min.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ h2 hpk(unsigned short lo, unsigned short hi) {
+  return (h2)lo | ((h2)hi << 16);
+}
+// c10::Half distance (dx*dx + dy*dy) + dz*dz on two lanes at once.
+__device__ __forceinline__ h2 hdist2(h2 dx, h2 dy, h2 dz) {
+  return hadd2r(hadd2r(hmul2r(dx, dx), hmul2r(dy, dy)), hmul2r(dz, dz));
+}
+
 __device__ __forceinline__ float min3f(float a, float b, float c) {
   float r;
   asm("min.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
