@@ -162,25 +162,35 @@ __global__ void __launch_bounds__(KW * 32)
 #pragma unroll
           for (int d = 0; d < DC; ++d) cc[d] = (cv && d < Dn) ? s_c[c][d] : T(0.0f);
           const int cidx = (int)(t0 + c);
+          // all distances and filters of the step first; one branch decides
+          // whether any query of this warp has a candidate at all
+          V dv[KQ];
+          unsigned bal[KQ];
+          unsigned any = 0;
 #pragma unroll
           for (int i = 0; i < KQ; ++i) {
-            if (!qv[i]) continue;  // warp-uniform
-            const V dv = knn_dist<T, DT, NORM, MODE>(q[i], cc, Dn);
-            unsigned bal = __ballot_sync(0xffffffffu, cv && dv < thr[i]);
-            while (bal) {
-              const int src = __ffs(bal) - 1;
-              bal &= bal - 1;
-              const V cd = __shfl_sync(0xffffffffu, dv, src);
-              if (cd < thr[i]) {
-                const int ci = cidx - lane + src;
-                const V upd = __shfl_up_sync(0xffffffffu, Ld[i], 1);
-                const int upi = __shfl_up_sync(0xffffffffu, Li[i], 1);
-                if (cd < Ld[i]) {
-                  const bool take_prev = lane > 0 && cd < upd;
-                  Ld[i] = take_prev ? upd : cd;
-                  Li[i] = take_prev ? upi : ci;
+            dv[i] = knn_dist<T, DT, NORM, MODE>(q[i], cc, Dn);
+            bal[i] = __ballot_sync(0xffffffffu, qv[i] && cv && dv[i] < thr[i]);
+            any |= bal[i];
+          }
+          if (any) {
+#pragma unroll
+            for (int i = 0; i < KQ; ++i) {
+              while (bal[i]) {
+                const int src = __ffs(bal[i]) - 1;
+                bal[i] &= bal[i] - 1;
+                const V cd = __shfl_sync(0xffffffffu, dv[i], src);
+                if (cd < thr[i]) {
+                  const int ci = cidx - lane + src;
+                  const V upd = __shfl_up_sync(0xffffffffu, Ld[i], 1);
+                  const int upi = __shfl_up_sync(0xffffffffu, Li[i], 1);
+                  if (cd < Ld[i]) {
+                    const bool take_prev = lane > 0 && cd < upd;
+                    Ld[i] = take_prev ? upd : cd;
+                    Li[i] = take_prev ? upi : ci;
+                  }
+                  thr[i] = __shfl_sync(0xffffffffu, Ld[i], K - 1);
                 }
-                thr[i] = __shfl_sync(0xffffffffu, Ld[i], K - 1);
               }
             }
           }
