@@ -22,8 +22,14 @@
 
 namespace tpo {
 
-constexpr int KQ = 8;        // queries per warp
-constexpr int KW = 4;        // warps per CTA
+#ifndef TPO_KQ
+#define TPO_KQ 4
+#endif
+constexpr int KQ = TPO_KQ;   // queries per warp
+#ifndef TPO_KW
+#define TPO_KW 8
+#endif
+constexpr int KW = TPO_KW;   // warps per CTA
 constexpr int KSTEP = 32;    // targets per step (one per lane)
 constexpr int KTILE = 256;   // targets per shared-memory tile
 constexpr int KDMAX = 8;
