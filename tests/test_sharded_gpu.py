@@ -12,7 +12,7 @@ import datagen
 pytestmark = pytest.mark.gpu
 
 
-def _run(rank, world, port, x1, x2, q):
+def _run(rank, world, port, x1, x2, q, dtype=torch.float32):
     import torch.distributed as dist
 
     import torch_point_ops_b200 as tpo
@@ -22,16 +22,17 @@ def _run(rank, world, port, x1, x2, q):
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
-    a, b = x1.to(dev), x2.to(dev)
+    a, b = x1.to(dev, dtype), x2.to(dev, dtype)
     loss, g1, g2 = sharded_chamfer_loss(a, b)
     if rank == 0:
         ra = a.clone().requires_grad_()
         rb = b.clone().requires_grad_()
         ref = tpo.ChamferDistance("mean")(ra, rb)
         ref.backward()
-        ok = (torch.allclose(loss, ref, rtol=1e-5) and
-              torch.allclose(g1, ra.grad, rtol=1e-5, atol=1e-10) and
-              torch.allclose(g2, rb.grad, rtol=1e-5, atol=1e-10))
+        rt, at = (1e-5, 1e-10) if dtype == torch.float32 else (1e-12, 1e-17)
+        ok = (torch.allclose(loss, ref, rtol=rt) and
+              torch.allclose(g1, ra.grad, rtol=rt, atol=at) and
+              torch.allclose(g2, rb.grad, rtol=rt, atol=at))
         q.put(bool(ok))
     dist.destroy_process_group()
 
@@ -44,8 +45,9 @@ def _port():
     return p
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float64])
 @pytest.mark.parametrize("world", [1, 2])
-def test_sharded_matches_single(world):
+def test_sharded_matches_single(world, dtype):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
@@ -55,7 +57,7 @@ def test_sharded_matches_single(world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_run, args=(r, world, port, x1, x2, q)) for r in range(world)]
+    procs = [ctx.Process(target=_run, args=(r, world, port, x1, x2, q, dtype)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:

@@ -43,10 +43,24 @@ def sharded_chamfer_loss(xyz1: torch.Tensor, xyz2: torch.Tensor, group=None, fla
     k1 = ops.chamfer_keys_empty(xyz1, B * N)
     k2 = ops.chamfer_keys_empty(xyz1, B * M)
     ops.chamfer_fwd_keys(xyz1, xyz2, r0, r1, flags, k1, k2)
+    if world > 1 and r1 == r0:
+        # a rank without rows folded nothing: its empty keys (all ones = -1 as a
+        # signed int64) must not win the signed MIN below
+        k2.fill_(torch.iinfo(torch.int64).max)
     if world > 1:
-        if k2.numel() != B * M:
-            raise NotImplementedError("sharded fp64 chamfer needs 128-bit key merging")
-        dist.all_reduce(k2, op=dist.ReduceOp.MIN, group=group)
+        if k2.numel() == B * M:  # 64-bit keys (fp32 / fp16): one element-wise MIN
+            dist.all_reduce(k2, op=dist.ReduceOp.MIN, group=group)
+        else:  # fp64: 128-bit keys {lo = index, hi = distance bits}; gather, then
+            # the lexicographic (hi, lo) minimum over ranks
+            allk = torch.empty((world,) + k2.shape, dtype=k2.dtype, device=k2.device)
+            dist.all_gather_into_tensor(allk, k2, group=group)
+            allk = allk.view(world, -1, 2)
+            hi = allk[..., 1]
+            best_hi = hi.min(dim=0).values
+            lo = torch.where(hi == best_hi, allk[..., 0],
+                             torch.full_like(allk[..., 0], torch.iinfo(torch.int64).max))
+            # keys are non-negative as int64 (distance >= 0, index < 2^31)
+            k2 = torch.stack([lo.min(dim=0).values, best_hi], dim=-1).reshape(-1)
     d1, d2, i1, i2 = ops.chamfer_finalize(xyz1, xyz2, r0, r1, flags, k1, k2)
     # loss: this rank's rows of dist1 + its column shard of dist2, summed over ranks
     part = d1[:, r0:r1].double().sum() / (B * N) + d2[:, c0:c1].double().sum() / (B * M)
