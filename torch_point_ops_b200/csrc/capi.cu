@@ -122,7 +122,10 @@ int tpo_chamfer_fwd(int dtype, int flags, const void* xyz1, const void* xyz2, in
   char* k1 = (char*)workspace;
   char* k2 = k1 + align256(kb * (size_t)B * (size_t)N);
   if (B > 0 && N > 0 && M > 0) {
-    if ((s = cuda_status(cudaMemsetAsync(workspace, 0xff, need, st)))) return s;
+    const size_t es = (size_t)dtype_size(dtype);
+    if ((s = fill_prefetch(workspace, need, nullptr, 0, 0xff, xyz1, es * 3 * B * N, xyz2,
+                           es * 3 * B * M, st)))
+      return s;
     if ((s = chamfer_fwd_keys(dtype, flags, xyz1, xyz2, B, N, M, 0, N, k1, k2, st))) return s;
   }
   return chamfer_finalize(dtype, flags, xyz1, xyz2, B, N, M, 0, N, k1, k2, dist1, idx1, dist2, idx2,
@@ -208,7 +211,10 @@ int tpo_chamfer_loss_fwd(int dtype, int flags, const void* xyz1, const void* xyz
   char* k2 = k1 + align256(kb * (size_t)B * (size_t)N);
   if (loss_uses_keys_kernel(dtype, B, N, M)) {
     // keys to the empty key and the reduction counters to 0xffffffff: one fill
-    if ((s = cuda_status(cudaMemsetAsync(w, 0xff, L.kl + keys_loss_counter_bytes(B), st)))) return s;
+    const size_t es = (size_t)dtype_size(dtype);
+    if ((s = fill_prefetch(w, L.kl + keys_loss_counter_bytes(B), nullptr, 0, 0xff, xyz1,
+                           es * 3 * B * N, xyz2, es * 3 * B * M, st)))
+      return s;
     return chamfer_loss_keys(dtype, flags, xyz1, xyz2, B, N, M, reduction, k1, k2, w + L.kl, loss, st);
   }
   if (L.kl && (s = cuda_status(cudaMemsetAsync(w, 0xff, L.kl, st)))) return s;
@@ -232,8 +238,9 @@ int tpo_chamfer_loss_bwd(int dtype, int flags, const void* xyz1, const void* xyz
     return fail(TPO_ERR_INVALID_ARGUMENT, "chamfer_loss_bwd: null pointer");
   cudaStream_t st = (cudaStream_t)stream;
   const size_t es = (size_t)dtype_size(dtype);
-  if (B * N > 0 && (s = cuda_status(cudaMemsetAsync(grad_xyz1, 0, es * 3 * B * N, st)))) return s;
-  if (B * M > 0 && (s = cuda_status(cudaMemsetAsync(grad_xyz2, 0, es * 3 * B * M, st)))) return s;
+  if ((s = fill_prefetch(grad_xyz1, es * 3 * B * N, grad_xyz2, es * 3 * B * M, 0, nullptr, 0,
+                         nullptr, 0, st)))
+    return s;
   const LossLayout L = loss_layout(dtype, B, N, M);
   const char* w = (const char*)workspace;
   if (loss_uses_keys_kernel(dtype, B, N, M)) {

@@ -129,3 +129,50 @@ int chamfer_bwd_accumulate(int dtype, const void* x1, const void* x2, int64_t B,
 }
 
 }  // namespace tpo
+
+namespace tpo {
+
+// Workspace / gradient initialisation as one kernel: fills up to two byte ranges
+// (16-byte stores where aligned) and, meanwhile, asks L2 to fetch up to two
+// input arrays (prefetch.global.L2: no register result, nothing waits on it) so
+// that the next kernel's first touches of its inputs hit L2.
+__global__ void fill_prefetch_kernel(unsigned char* d0, size_t n0, unsigned char* d1, size_t n1,
+                                     unsigned v32, const char* p0, size_t m0, const char* p1,
+                                     size_t m1) {
+  const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  const size_t nth = (size_t)gridDim.x * blockDim.x;
+  const uint4 v = make_uint4(v32, v32, v32, v32);
+  for (int r = 0; r < 2; ++r) {
+    unsigned char* d = r ? d1 : d0;
+    const size_t n = r ? n1 : n0;
+    if (!d || !n) continue;
+    size_t head = (16 - ((uintptr_t)d & 15)) & 15;
+    if (head > n) head = n;
+    for (size_t i = tid; i < head; i += nth) d[i] = (unsigned char)v32;
+    const size_t nv = (n - head) / 16;
+    uint4* dv = reinterpret_cast<uint4*>(d + head);
+    for (size_t i = tid; i < nv; i += nth) dv[i] = v;
+    for (size_t i = head + nv * 16 + tid; i < n; i += nth) d[i] = (unsigned char)v32;
+  }
+  for (int r = 0; r < 2; ++r) {
+    const char* p = r ? p1 : p0;
+    const size_t m = r ? m1 : m0;
+    if (!p) continue;
+    for (size_t i = tid * 128; i < m; i += nth * 128)
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(p + i));
+  }
+}
+
+int fill_prefetch(void* d0, size_t n0, void* d1, size_t n1, unsigned char value, const void* p0,
+                  size_t m0, const void* p1, size_t m1, cudaStream_t st) {
+  const size_t work = std::max(n0 + n1, (m0 + m1) / 8);
+  if (work == 0) return TPO_OK;
+  const int threads = 256;
+  const unsigned blocks = (unsigned)std::min<size_t>((work / 16 + threads - 1) / threads + 1, 148 * 4);
+  const unsigned v32 = value * 0x01010101u;
+  fill_prefetch_kernel<<<blocks, threads, 0, st>>>((unsigned char*)d0, n0, (unsigned char*)d1, n1,
+                                                   v32, (const char*)p0, m0, (const char*)p1, m1);
+  return check_launch();
+}
+
+}  // namespace tpo
