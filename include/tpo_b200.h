@@ -58,6 +58,14 @@ enum tpo_status {
 TPO_API const char* tpo_status_string(int status);
 TPO_API int tpo_abi_version(void);
 
+/* Device-side error flags of the current device (no counterpart in the
+ * reference, which has no bounded waits): kernels never spin forever; a wait for
+ * a bulk copy into shared memory that gives up sets bit 0
+ * (TPO_DEVERR_BULK_TIMEOUT) and the kernel continues.  Reads the flags into
+ * *flags (synchronous) and clears them if `clear` is non-zero. */
+enum tpo_device_errors { TPO_DEVERR_BULK_TIMEOUT = 1 };
+TPO_API int tpo_device_error_flags(unsigned* flags, int clear);
+
 /* ------------------------------------------------------------------------- */
 /* Chamfer distance forward.  Replaces chamfer_cuda_forward
  * (torch_point_ops/chamfer/csrc/cuda/chamfer.cu:169-198) behind the

@@ -47,6 +47,11 @@ const char* tpo_status_string(int status) {
   return "unknown status";
 }
 
+int tpo_device_error_flags(unsigned* flags, int clear) {
+  if (!flags) return fail(TPO_ERR_INVALID_ARGUMENT, "device_error_flags: null output");
+  return device_error_flags(flags, clear != 0);
+}
+
 int tpo_chamfer_key_bytes(int dtype) {
   if (!valid_dtype(dtype)) return 0;
   return dtype == TPO_F64 ? 16 : 8;

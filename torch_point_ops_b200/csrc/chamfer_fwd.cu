@@ -32,6 +32,9 @@
 namespace tpo {
 
 // ----------------------------- fp32 fast path -----------------------------
+// Set (kErrBulkTimeout) if a bounded wait for a bulk copy ever gave up; read by
+// tpo_device_error_flags().
+static __device__ unsigned g_fwd_device_error = 0;
 #ifndef TPO_CF_R
 #define TPO_CF_R 16
 #endif
@@ -190,33 +193,50 @@ __global__ void __launch_bounds__(CF_MAXW * 32, TPO_CF_MINB)
   const int n_active = (int)min64(W, (row_end - blk_row0 + CF_ROWS_PER_WARP - 1) / CF_ROWS_PER_WARP);
   const float qnan = __int_as_float(0x7fffffff);
 
-  // The CTA's rows, staged once (coalesced) in shared memory: lanes read their
-  // R rows from here, and the column merge rescans winning row chunks here.
+  // The CTA's rows, staged once in shared memory (lanes read their R rows from
+  // here; the column merge rescans winning row chunks here), and each column
+  // tile, land by 1-D bulk copies (TMA) on one mbarrier; unaligned heads/tails
+  // and NaN padding are filled by plain loads meanwhile.
   __shared__ __align__(16) float s_rows[CF_MAXW * CF_ROWS_PER_WARP * 3];
-  {
-    const int64_t nrow = min64((int64_t)W * CF_ROWS_PER_WARP, max64(row_end - blk_row0, 0));
-    const float* src = xyz1 + (b * N + blk_row0) * 3;
-#pragma unroll 8
-    for (int e = threadIdx.x; e < W * CF_ROWS_PER_WARP * 3; e += blockDim.x)
-      s_rows[e] = e < nrow * 3 ? __ldg(src + e) : qnan;
-  }
-  // a column tile: xyz2[tc, tc+256) of this batch, duplicated {c,c}, NaN-padded to
-  // a whole number of 8-column chunks
-  auto stage_tile = [&](int64_t tc) {
+  __shared__ __align__(16) float s_raw[CF_TILE * 3];
+  __shared__ __align__(8) unsigned long long s_bar;
+  unsigned phase = 0;
+  if (threadIdx.x == 0) mbar_init(&s_bar, 1);
+  __syncthreads();
+  const int64_t nrow = min64((int64_t)W * CF_ROWS_PER_WARP, max64(row_end - blk_row0, 0));
+  auto stage = [&](bool with_rows, int64_t tc) {
+    const float* rsrc = xyz1 + (b * N + blk_row0) * 3;
+    const int rfl = with_rows ? (int)(nrow * 3) : 0;  // row floats to load
+    const int rbulk = (((uintptr_t)rsrc & 15) == 0) ? (rfl & ~3) : 0;
     const int ncols = (int)min64(CF_TILE, c1 - tc);
+    const float* tsrc = xyz2 + (b * M + tc) * 3;
+    const int tfl = ncols * 3;
+    const int tbulk = (((uintptr_t)tsrc & 15) == 0) ? (tfl & ~3) : 0;
+    if (threadIdx.x == 0) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      mbar_expect_tx(&s_bar, (unsigned)(rbulk + tbulk) * 4u);
+      if (rbulk) bulk_g2s(s_rows, rsrc, (unsigned)rbulk * 4u, &s_bar);
+      if (tbulk) bulk_g2s(s_raw, tsrc, (unsigned)tbulk * 4u, &s_bar);
+    }
+    if (with_rows)
+      for (int e = rbulk + threadIdx.x; e < W * CF_ROWS_PER_WARP * 3; e += blockDim.x)
+        s_rows[e] = e < rfl ? __ldg(rsrc + e) : qnan;
+    for (int e = tbulk + threadIdx.x; e < tfl; e += blockDim.x) s_raw[e] = __ldg(tsrc + e);
+    mbar_wait(&s_bar, phase, &g_fwd_device_error);
+    phase ^= 1u;
+    __syncthreads();
+    // duplicated {c,c} layout, NaN-padded to whole 8-column chunks
     const int nsteps = ((ncols + CF_CHUNK - 1) / CF_CHUNK) * 2;
-    const float* src = xyz2 + (b * M + tc) * 3;
     float2* dst = &s_col[0][0][0];
-#pragma unroll 4
     for (int e = threadIdx.x; e < nsteps * CF_C * 3; e += blockDim.x) {
       const int col = e / 3;
       const int comp = e - col * 3;
-      const float v = col < ncols ? __ldg(src + e) : qnan;
+      const float v = col < ncols ? s_raw[e] : qnan;
       dst[((col >> 2) * 3 + comp) * CF_C + (col & 3)] = make_float2(v, v);
     }
+    __syncthreads();
   };
-  if (c0 < c1) stage_tile(c0);
-  __syncthreads();
+  if (c0 < c1) stage(true, c0);
   u64 QX[CF_RP], QY[CF_RP], QZ[CF_RP];
   {
     const float* a = s_rows + (warp * CF_ROWS_PER_WARP + lane * CF_R) * 3;
@@ -240,8 +260,7 @@ __global__ void __launch_bounds__(CF_MAXW * 32, TPO_CF_MINB)
     const int nsteps = ((ncols + CF_CHUNK - 1) / CF_CHUNK) * 2;  // even: 8-column chunks
     if (tc != c0) {  // the first tile was staged together with the rows
       __syncthreads();
-      stage_tile(tc);
-      __syncthreads();
+      stage(false, tc);
     }
     if (warp_active) {
       // Two 4-column sub-steps per iteration; the row-side chunk is 8 columns.
@@ -976,13 +995,13 @@ Plan make_plan(int64_t B, int64_t nrows, int64_t M, int rows_per_warp, int max_w
   p.warps = (int)std::max<int64_t>(1, std::min<int64_t>(max_warps, warps_needed));
   p.rb_count = (int)((warps_needed + p.warps - 1) / p.warps);
   const int64_t base = B * p.rb_count;
-  const int64_t max_cs = std::max<int64_t>(1, (M + 63) / 64);
+  const int64_t max_cs = std::max<int64_t>(1, (M + 7) / 8);  // segments of >= one 8-column chunk
   // cost model: waves * (columns per unit + fixed overhead in column units)
   double best = 1e300;
   int64_t best_cs = 1;
   const int64_t lim = std::min<int64_t>(max_cs, 4096);
   for (int64_t cs = 1; cs <= lim; ++cs) {
-    const int64_t seg = ((M + cs - 1) / cs + 3) / 4 * 4;
+    const int64_t seg = ((M + cs - 1) / cs + 7) / 8 * 8;
     const int64_t real_cs = (M + seg - 1) / seg;
     if (real_cs != cs) continue;
     const int64_t units = base * cs;
@@ -993,7 +1012,7 @@ Plan make_plan(int64_t B, int64_t nrows, int64_t M, int rows_per_warp, int max_w
       best_cs = cs;
     }
   }
-  p.seg = std::max<int64_t>(4, ((M + best_cs - 1) / best_cs + 3) / 4 * 4);
+  p.seg = std::max<int64_t>(8, ((M + best_cs - 1) / best_cs + 7) / 8 * 8);
   p.cs_count = (int)((M + p.seg - 1) / p.seg);
   p.ctas = base * p.cs_count;
   return p;
@@ -1160,6 +1179,13 @@ int chamfer_bwd_from_keys(int dtype, int flags, const void* x1, const void* x2, 
         (const float*)x1, (const float*)x2, B, N, M, K1, K2, (const float*)grad_loss, reduction,
         (float*)gx1, (float*)gx2);
   return check_launch();
+}
+
+int device_error_flags(unsigned* out, bool clear) {
+  int s = cuda_status(cudaMemcpyFromSymbol(out, g_fwd_device_error, sizeof(unsigned)));
+  if (s || !clear) return s;
+  const unsigned zero = 0;
+  return cuda_status(cudaMemcpyToSymbol(g_fwd_device_error, &zero, sizeof(unsigned)));
 }
 
 }  // namespace tpo

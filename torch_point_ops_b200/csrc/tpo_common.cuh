@@ -199,6 +199,48 @@ __device__ __forceinline__ void key128_min(Key128* addr, u64 hi, u64 lo) {
 __host__ __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
 __host__ __device__ __forceinline__ int64_t max64(int64_t a, int64_t b) { return a > b ? a : b; }
 
+// ---- 1-D bulk copies global -> shared (the TMA unit's non-tensor form) ----
+// One thread issues a copy of `bytes` (multiple of 16; both addresses 16-byte
+// aligned) that completes on an mbarrier as transaction bytes.  The wait is
+// bounded: after kBulkWaitLimit polls it ORs kErrBulkTimeout into *err and
+// returns false instead of spinning forever.
+constexpr unsigned kBulkWaitLimit = 1u << 24;
+constexpr unsigned kErrBulkTimeout = 1u;
+
+__device__ __forceinline__ unsigned smem_addr(const void* p) {
+  return (unsigned)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(unsigned long long* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(unsigned long long* bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes,
+                                         unsigned long long* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+__device__ __forceinline__ bool mbar_wait(unsigned long long* bar, unsigned parity, unsigned* err) {
+  for (unsigned it = 0; it < kBulkWaitLimit; ++it) {
+    unsigned done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  atomicOr(err, kErrBulkTimeout);
+  return false;
+}
+
 __device__ __forceinline__ unsigned lane_id() {
   unsigned r;
   asm("mov.u32 %0, %%laneid;" : "=r"(r));

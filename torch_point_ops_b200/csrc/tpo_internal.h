@@ -61,6 +61,9 @@ int chamfer_bwd_from_keys(int dtype, int flags, const void* x1, const void* x2, 
 int fill_prefetch(void* d0, size_t n0, void* d1, size_t n1, unsigned char value, const void* p0,
                   size_t m0, const void* p1, size_t m1, cudaStream_t st);
 
+// Reads (and optionally clears) the device-side error flags of this device.
+int device_error_flags(unsigned* out, bool clear);
+
 inline int dtype_size(int dtype) {
   return dtype == TPO_F32 ? 4 : dtype == TPO_F16 ? 2 : dtype == TPO_F64 ? 8 : 0;
 }
