@@ -63,3 +63,7 @@ def test_empty_problem_is_a_noop():
     rc = lib().tpo_chamfer_fwd(0, 0, VP(0), VP(0), I64(0), I64(5), I64(5), VP(0), VP(0),
                                VP(0), VP(0), VP(0), ctypes.c_size_t(0), VP(0))
     assert rc == 0
+
+
+def test_device_error_flags_null_rejected():
+    assert lib().tpo_device_error_flags(VP(0), 0) == 1

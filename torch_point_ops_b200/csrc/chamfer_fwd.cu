@@ -386,28 +386,46 @@ __global__ void __launch_bounds__(CF_MAXW * 32, TPO_CF_MINB)
   const int n_active = (int)min64(W, (row_end - blk_row0 + CF_ROWS_PER_WARP - 1) / CF_ROWS_PER_WARP);
   const unsigned short hnan = 0x7fff;
 
-  {
-    const int64_t nrow = min64((int64_t)W * CF_ROWS_PER_WARP, max64(row_end - blk_row0, 0));
-    const __half* src = xyz1 + (b * N + blk_row0) * 3;
-#pragma unroll 8
-    for (int e = threadIdx.x; e < W * CF_ROWS_PER_WARP * 3; e += blockDim.x)
-      s_rows[e] = e < nrow * 3 ? src[e] : __ushort_as_half(hnan);
-  }
-  auto stage_tile = [&](int64_t tc) {
+  // rows and column tiles by 1-D bulk copies on one mbarrier (as the fp32 kernel)
+  __shared__ __align__(16) unsigned short s_raw[CF_TILE * 3];
+  __shared__ __align__(8) unsigned long long s_bar;
+  unsigned phase = 0;
+  if (threadIdx.x == 0) mbar_init(&s_bar, 1);
+  __syncthreads();
+  const int64_t nrow = min64((int64_t)W * CF_ROWS_PER_WARP, max64(row_end - blk_row0, 0));
+  unsigned short* s_rows16 = reinterpret_cast<unsigned short*>(s_rows);
+  auto stage = [&](bool with_rows, int64_t tc) {
+    const unsigned short* rsrc = reinterpret_cast<const unsigned short*>(xyz1 + (b * N + blk_row0) * 3);
+    const int rfl = with_rows ? (int)(nrow * 3) : 0;
+    const int rbulk = (((uintptr_t)rsrc & 15) == 0) ? (rfl & ~7) : 0;
     const int ncols = (int)min64(CF_TILE, c1 - tc);
+    const unsigned short* tsrc = reinterpret_cast<const unsigned short*>(xyz2 + (b * M + tc) * 3);
+    const int tfl = ncols * 3;
+    const int tbulk = (((uintptr_t)tsrc & 15) == 0) ? (tfl & ~7) : 0;
+    if (threadIdx.x == 0) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      mbar_expect_tx(&s_bar, (unsigned)(rbulk + tbulk) * 2u);
+      if (rbulk) bulk_g2s(s_rows16, rsrc, (unsigned)rbulk * 2u, &s_bar);
+      if (tbulk) bulk_g2s(s_raw, tsrc, (unsigned)tbulk * 2u, &s_bar);
+    }
+    if (with_rows)
+      for (int e = rbulk + threadIdx.x; e < W * CF_ROWS_PER_WARP * 3; e += blockDim.x)
+        s_rows16[e] = e < rfl ? rsrc[e] : hnan;
+    for (int e = tbulk + threadIdx.x; e < tfl; e += blockDim.x) s_raw[e] = tsrc[e];
+    mbar_wait(&s_bar, phase, &g_fwd_device_error);
+    phase ^= 1u;
+    __syncthreads();
     const int nsteps = ((ncols + CF_CHUNK - 1) / CF_CHUNK) * 2;
-    const unsigned short* src = reinterpret_cast<const unsigned short*>(xyz2 + (b * M + tc) * 3);
     h2* dst = &s_col[0][0][0];
-#pragma unroll 4
     for (int e = threadIdx.x; e < nsteps * CF_C * 3; e += blockDim.x) {
       const int col = e / 3;
       const int comp = e - col * 3;
-      const unsigned short v = col < ncols ? src[e] : hnan;
+      const unsigned short v = col < ncols ? s_raw[e] : hnan;
       dst[((col >> 2) * 3 + comp) * CF_C + (col & 3)] = hpk(v, v);
     }
+    __syncthreads();
   };
-  if (c0 < c1) stage_tile(c0);
-  __syncthreads();
+  if (c0 < c1) stage(true, c0);
   h2 QX[CF_RP], QY[CF_RP], QZ[CF_RP];
   {
     const unsigned short* a = reinterpret_cast<const unsigned short*>(s_rows) +
@@ -431,8 +449,7 @@ __global__ void __launch_bounds__(CF_MAXW * 32, TPO_CF_MINB)
     const int nsteps = ((ncols + CF_CHUNK - 1) / CF_CHUNK) * 2;
     if (tc != c0) {
       __syncthreads();
-      stage_tile(tc);
-      __syncthreads();
+      stage(false, tc);
     }
     if (warp_active) {
 #pragma unroll 1
