@@ -220,7 +220,8 @@ int tpo_chamfer_loss_fwd(int dtype, int flags, const void* xyz1, const void* xyz
     if ((s = fill_prefetch(w, L.kl + keys_loss_counter_bytes(B), nullptr, 0, 0xff, xyz1,
                            es * 3 * B * N, xyz2, es * 3 * B * M, st)))
       return s;
-    return chamfer_loss_keys(dtype, flags, xyz1, xyz2, B, N, M, reduction, k1, k2, w + L.kl, loss, st);
+    return chamfer_loss_keys(dtype, flags, xyz1, xyz2, B, N, M, reduction, k1, k2, w + L.kl, loss,
+                             w + L.fin, st);
   }
   if (L.kl && (s = cuda_status(cudaMemsetAsync(w, 0xff, L.kl, st)))) return s;
   if ((s = cuda_status(cudaMemsetAsync(w + L.fin + kFinPartialBytes, 0xff, 256, st)))) return s;

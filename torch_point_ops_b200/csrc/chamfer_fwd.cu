@@ -72,19 +72,6 @@ __device__ __forceinline__ float col_min(const float* v) {
   }
 }
 
-// Fused ChamferDistance reduction inside the keys kernel: the last CTA of each
-// batch (per-batch counter) sums that batch's final keys -- their high words are
-// the distances -- in a fixed order, and the last batch folds the per-batch sums
-// in batch order.  Deterministic; counters start at 0xffffffff.
-struct KeysLoss {
-  unsigned* batch_ctr;  // [B]
-  unsigned* glob_ctr;   // [1]
-  double* batch_part;   // [2B]
-  void* loss;           // nullptr: no fused loss
-  int reduction;        // 0 mean(d1)+mean(d2), 1 sum(d1)+sum(d2)
-  int half_out;         // loss is fp16 (else fp32)
-};
-
 __device__ __forceinline__ void block_sum2(double& a, double& c, double* sa, double* sc) {
 #pragma unroll
   for (int off = 16; off; off >>= 1) {
@@ -100,71 +87,10 @@ __device__ __forceinline__ void block_sum2(double& a, double& c, double* sa, dou
   for (int w = 0; w < (int)(blockDim.x >> 5); ++w) { a += sa[w]; c += sc[w]; }
 }
 
-// Sum of the distances held in n keys by this block, in a fixed order: 32
-// independent loads in flight per thread (the loads, not the adds, set the time).
-__device__ __forceinline__ double sum_key_values(const u64* k, int64_t n) {
-  constexpr int U = 32;
-  double acc[U];
-#pragma unroll
-  for (int u = 0; u < U; ++u) acc[u] = 0.0;
-  const int64_t stride = (int64_t)blockDim.x * U;
-  for (int64_t i0 = threadIdx.x; i0 < n; i0 += stride) {
-    u64 v[U];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int64_t i = i0 + (int64_t)u * blockDim.x;
-      v[u] = i < n ? __ldcg(k + i) : 0ull;
-    }
-#pragma unroll
-    for (int u = 0; u < U; ++u) acc[u] += (double)__uint_as_float((unsigned)(v[u] >> 32));
-  }
-  double t = 0.0;
-#pragma unroll
-  for (int u = 0; u < U; ++u) t += acc[u];
-  return t;
-}
-
 __device__ __forceinline__ unsigned atom_add_acq_rel(unsigned* p, unsigned v) {
   unsigned old;
   asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
   return old;
-}
-
-__device__ void keys_loss_epilogue(const KeysLoss& kl, const u64* keys1, const u64* keys2,
-                                   int64_t b, int64_t B, int64_t N, int64_t M, int per_batch) {
-  __shared__ double sa[CF_MAXW], sc[CF_MAXW];
-  __shared__ bool s_last;
-  // The barrier orders every thread's key reductions before thread 0's
-  // acq_rel counter update (release is cumulative); the last CTA's acquire,
-  // carried to its other threads by the next barrier, makes all CTAs' keys visible.
-  __syncthreads();
-  if (threadIdx.x == 0) s_last = atom_add_acq_rel(kl.batch_ctr + b, 1u) == (unsigned)(per_batch - 2);
-  __syncthreads();
-  if (!s_last) return;
-  double a = sum_key_values(keys1 + b * N, N), c = sum_key_values(keys2 + b * M, M);
-  block_sum2(a, c, sa, sc);
-  __shared__ bool s_glob;
-  if (threadIdx.x == 0) {
-    __stcg(kl.batch_part + 2 * b, a);
-    __stcg(kl.batch_part + 2 * b + 1, c);
-    s_glob = atom_add_acq_rel(kl.glob_ctr, 1u) == (unsigned)(B - 2);
-  }
-  __syncthreads();
-  if (!s_glob) return;
-  double ta = 0.0, tc = 0.0;
-  for (int64_t k = threadIdx.x; k < B; k += blockDim.x) {
-    ta += __ldcg(kl.batch_part + 2 * k);
-    tc += __ldcg(kl.batch_part + 2 * k + 1);
-  }
-  block_sum2(ta, tc, sa, sc);
-  if (threadIdx.x != 0) return;
-  // torch semantics: each mean (or sum) rounded to float, then added in float
-  const double v1 = kl.reduction == 0 ? ta / (double)(B * N) : ta;
-  const double v2 = kl.reduction == 0 ? tc / (double)(B * M) : tc;
-  if (kl.half_out)  // c10::Half: each term rounded to half, added with half rounding
-    *(__half*)kl.loss = hadd_rn(__float2half_rn((float)v1), __float2half_rn((float)v2));
-  else
-    *(float*)kl.loss = __fadd_rn((float)v1, (float)v2);
 }
 
 template <int MODE>
@@ -172,7 +98,7 @@ __global__ void __launch_bounds__(CF_MAXW * 32, TPO_CF_MINB)
     chamfer_keys_f32_kernel(const float* __restrict__ xyz1, const float* __restrict__ xyz2,
                             int64_t N, int64_t M, int64_t row_begin, int64_t row_end,
                             int rb_count, int cs_count, int64_t seg,
-                            u64* __restrict__ keys1, u64* __restrict__ keys2, KeysLoss kl) {
+                            u64* __restrict__ keys1, u64* __restrict__ keys2) {
   __shared__ __align__(16) float2 s_col[CF_TILE_STEPS][3][CF_C];
   __shared__ __align__(16) uint2 s_wb[CF_MAXW][CF_TILE];  // {ballot, distance bits}
 
@@ -342,9 +268,6 @@ __global__ void __launch_bounds__(CF_MAXW * 32, TPO_CF_MINB)
                     ((u64)__float_as_uint(best[r]) << 32) | (unsigned)bchunk[r]);
     }
   }
-  if (kl.loss != nullptr)
-    keys_loss_epilogue(kl, keys1, keys2, b, (int64_t)gridDim.x / (rb_count * cs_count), N, M,
-                       rb_count * cs_count);
 }
 
 // ----------------------------- fp16 fast path -----------------------------
@@ -364,7 +287,7 @@ __global__ void __launch_bounds__(CF_MAXW * 32, TPO_CF_MINB)
     chamfer_keys_f16_kernel(const __half* __restrict__ xyz1, const __half* __restrict__ xyz2,
                             int64_t N, int64_t M, int64_t row_begin, int64_t row_end,
                             int rb_count, int cs_count, int64_t seg,
-                            u64* __restrict__ keys1, u64* __restrict__ keys2, KeysLoss kl) {
+                            u64* __restrict__ keys1, u64* __restrict__ keys2) {
   __shared__ __align__(16) h2 s_col[CF_TILE_STEPS][3][CF_C];
   __shared__ __align__(16) uint2 s_wb[CF_MAXW][CF_TILE];  // {ballot, half distance bits}
   __shared__ __align__(16) __half s_rows[CF_MAXW * CF_ROWS_PER_WARP * 3];
@@ -533,9 +456,6 @@ __global__ void __launch_bounds__(CF_MAXW * 32, TPO_CF_MINB)
       }
     }
   }
-  if (kl.loss != nullptr)
-    keys_loss_epilogue(kl, keys1, keys2, b, (int64_t)gridDim.x / (rb_count * cs_count), N, M,
-                       rb_count * cs_count);
 }
 
 // ------------------------- fp16 / fp64 generic path -------------------------
@@ -1047,8 +967,7 @@ int slots_for(KernelT kernel, int threads) {
 
 template <int MODE>
 int launch_keys_f32(const float* x1, const float* x2, int64_t B, int64_t N, int64_t M,
-                    int64_t rb0, int64_t rb1, void* k1, void* k2, cudaStream_t st,
-                    KeysLoss kl = KeysLoss{nullptr, nullptr, nullptr, nullptr, 0, 0}) {
+                    int64_t rb0, int64_t rb1, void* k1, void* k2, cudaStream_t st) {
   auto kern = chamfer_keys_f32_kernel<MODE>;
   static thread_local int slots_cache[64] = {0};
   int dev = 0;
@@ -1058,13 +977,12 @@ int launch_keys_f32(const float* x1, const float* x2, int64_t B, int64_t N, int6
   const Plan p = make_plan(B, rb1 - rb0, M, CF_ROWS_PER_WARP, CF_MAXW, slots);
   if (p.ctas <= 0) return TPO_OK;
   kern<<<(unsigned)p.ctas, p.warps * 32, 0, st>>>(x1, x2, N, M, rb0, rb1, p.rb_count, p.cs_count,
-                                                   p.seg, (u64*)k1, (u64*)k2, kl);
+                                                   p.seg, (u64*)k1, (u64*)k2);
   return check_launch();
 }
 
 int launch_keys_f16(const __half* x1, const __half* x2, int64_t B, int64_t N, int64_t M,
-                    int64_t rb0, int64_t rb1, void* k1, void* k2, cudaStream_t st,
-                    KeysLoss kl = KeysLoss{nullptr, nullptr, nullptr, nullptr, 0, 0}) {
+                    int64_t rb0, int64_t rb1, void* k1, void* k2, cudaStream_t st) {
   auto kern = chamfer_keys_f16_kernel;
   static thread_local int slots_cache[64] = {0};
   int dev = 0;
@@ -1074,7 +992,7 @@ int launch_keys_f16(const __half* x1, const __half* x2, int64_t B, int64_t N, in
   const Plan p = make_plan(B, rb1 - rb0, M, CF_ROWS_PER_WARP, CF_MAXW, slots);
   if (p.ctas <= 0) return TPO_OK;
   kern<<<(unsigned)p.ctas, p.warps * 32, 0, st>>>(x1, x2, N, M, rb0, rb1, p.rb_count, p.cs_count,
-                                                   p.seg, (u64*)k1, (u64*)k2, kl);
+                                                   p.seg, (u64*)k1, (u64*)k2);
   return check_launch();
 }
 
@@ -1155,21 +1073,67 @@ int chamfer_finalize(int dtype, int flags, const void* x1, const void* x2, int64
   return TPO_ERR_INVALID_ARGUMENT;
 }
 
+// Loss from the final keys in a separate small kernel: grid-stride sums of the
+// row and column distances (fixed per-thread order), block partials, and the
+// last block folds them in block order -- deterministic for a given grid.
+// Cheaper than the keys kernel's per-batch last-CTA epilogue, whose serial
+// chain of counter atomics and loads sat at the end of the critical path.
+__global__ void keys_loss_reduce_kernel(const u64* __restrict__ k1, int64_t n1,
+                                        const u64* __restrict__ k2, int64_t n2,
+                                        double* __restrict__ part, unsigned* ctr, void* loss,
+                                        int half_out, int reduction) {
+  __shared__ double sa[32], sc[32];
+  double a = 0.0, c = 0.0;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n1;
+       i += (int64_t)gridDim.x * blockDim.x)
+    a += (double)__uint_as_float((unsigned)(__ldg(k1 + i) >> 32));
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n2;
+       i += (int64_t)gridDim.x * blockDim.x)
+    c += (double)__uint_as_float((unsigned)(__ldg(k2 + i) >> 32));
+  block_sum2(a, c, sa, sc);
+  __shared__ bool s_last;
+  if (threadIdx.x == 0) {
+    __stcg(part + 2 * blockIdx.x, a);
+    __stcg(part + 2 * blockIdx.x + 1, c);
+    s_last = atom_add_acq_rel(ctr, 1u) == gridDim.x - 2u;  // counter starts at 0xffffffff
+  }
+  __syncthreads();
+  if (!s_last) return;
+  a = 0.0;
+  c = 0.0;
+  for (unsigned k = threadIdx.x; k < gridDim.x; k += blockDim.x) {
+    a += __ldcg(part + 2 * k);
+    c += __ldcg(part + 2 * k + 1);
+  }
+  block_sum2(a, c, sa, sc);
+  if (threadIdx.x != 0) return;
+  const double v1 = reduction == 0 ? a / (double)n1 : a;
+  const double v2 = reduction == 0 ? c / (double)n2 : c;
+  if (half_out)
+    *(__half*)loss = hadd_rn(__float2half_rn((float)v1), __float2half_rn((float)v2));
+  else
+    *(float*)loss = __fadd_rn((float)v1, (float)v2);
+}
+
 int chamfer_loss_keys(int dtype, int flags, const void* x1, const void* x2, int64_t B, int64_t N,
                       int64_t M, int reduction, void* k1, void* k2, void* lossws, void* loss,
-                      cudaStream_t st) {
-  KeysLoss kl;
-  kl.batch_ctr = (unsigned*)lossws;
-  kl.glob_ctr = kl.batch_ctr + B;
-  kl.batch_part = (double*)((char*)lossws + keys_loss_counter_bytes(B));
-  kl.loss = loss;
-  kl.half_out = dtype == TPO_F16;
-  kl.reduction = reduction;
+                      void* partials, cudaStream_t st) {
+  int s;
   if (dtype == TPO_F16)
-    return launch_keys_f16((const __half*)x1, (const __half*)x2, B, N, M, 0, N, k1, k2, st, kl);
-  const bool exact = (flags & TPO_ROUND_EXACT) != 0;
-  return exact ? launch_keys_f32<TPO_ROUND_EXACT>((const float*)x1, (const float*)x2, B, N, M, 0, N, k1, k2, st, kl)
-               : launch_keys_f32<TPO_ROUND_FMA>((const float*)x1, (const float*)x2, B, N, M, 0, N, k1, k2, st, kl);
+    s = launch_keys_f16((const __half*)x1, (const __half*)x2, B, N, M, 0, N, k1, k2, st);
+  else if (flags & TPO_ROUND_EXACT)
+    s = launch_keys_f32<TPO_ROUND_EXACT>((const float*)x1, (const float*)x2, B, N, M, 0, N, k1, k2, st);
+  else
+    s = launch_keys_f32<TPO_ROUND_FMA>((const float*)x1, (const float*)x2, B, N, M, 0, N, k1, k2, st);
+  if (s) return s;
+  const int threads = 256;
+  const int64_t want = (B * (N + M) + threads * 8 - 1) / (threads * 8);
+  const unsigned blocks = (unsigned)std::max<int64_t>(1, std::min<int64_t>(want, 296));
+  unsigned* ctr = (unsigned*)lossws + B;  // the 0xff-filled counter word after the batch counters
+  keys_loss_reduce_kernel<<<blocks, threads, 0, st>>>((const u64*)k1, B * N, (const u64*)k2, B * M,
+                                                      (double*)partials, ctr, loss,
+                                                      dtype == TPO_F16, reduction);
+  return check_launch();
 }
 
 int chamfer_bwd_from_keys(int dtype, int flags, const void* x1, const void* x2, int64_t B,

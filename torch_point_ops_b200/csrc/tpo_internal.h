@@ -45,13 +45,14 @@ int knn_gather_backward(int dtype, const void* gout, const int64_t* idx, const i
                         int64_t N, int64_t M, int64_t U, int64_t L, int64_t K, void* gx,
                         cudaStream_t st);
 
-// Fused-loss forward on the fp32 keys kernel (rows 0..N, all columns).  lossws:
-// keys_loss_bytes(B) bytes whose first keys_loss_counter_bytes(B) are 0xff-filled.
+// Fused-loss forward: keys kernel (rows 0..N, all columns) + keys reduction.
+// lossws: keys_loss_bytes(B) bytes whose first keys_loss_counter_bytes(B) are
+// 0xff-filled (word B is the reduction's counter); partials: >= 296*16 bytes.
 inline size_t keys_loss_counter_bytes(int64_t B) { return ((size_t)(B + 1) * 4 + 255) & ~(size_t)255; }
 inline size_t keys_loss_bytes(int64_t B) { return keys_loss_counter_bytes(B) + (((size_t)B * 16 + 255) & ~(size_t)255); }
 int chamfer_loss_keys(int dtype, int flags, const void* x1, const void* x2, int64_t B, int64_t N,
                       int64_t M, int reduction, void* k1, void* k2, void* lossws, void* loss,
-                      cudaStream_t st);
+                      void* partials, cudaStream_t st);
 int chamfer_bwd_from_keys(int dtype, int flags, const void* x1, const void* x2, int64_t B, int64_t N,
                               int64_t M, const void* k1, const void* k2, const void* grad_loss,
                               int reduction, void* gx1, void* gx2, cudaStream_t st);
