@@ -149,6 +149,7 @@ class ChamferLossFn : public torch::autograd::Function<ChamferLossFn> {
     ctx->saved_data["reduction"] = reduction;
     ctx->saved_data["flags"] = flags;
     ctx->mark_non_differentiable({std::get<1>(out)});
+    ctx->set_materialize_grads(false);  // no zero-filled grad for the state output
     return {std::get<0>(out), std::get<1>(out)};
   }
   static torch::autograd::variable_list backward(torch::autograd::AutogradContext* ctx,
