@@ -18,6 +18,8 @@
 // Backward replaces KNearestNeighborBackwardKernel (knn.cu:401-466): one thread
 // per query row sums its K terms in k order (deterministic, no atomics for
 // grad_p1) and scatters the negated terms into grad_p2 with atomics.
+#include <type_traits>
+
 #include "tpo_internal.h"
 
 namespace tpo {
@@ -31,7 +33,10 @@ constexpr int KQ = TPO_KQ;   // queries per warp
 #endif
 constexpr int KW = TPO_KW;   // warps per CTA
 constexpr int KSTEP = 32;    // targets per step (one per lane)
-constexpr int KTILE = 256;   // targets per shared-memory tile
+#ifndef TPO_KTILE
+#define TPO_KTILE 2048
+#endif
+constexpr int KTILE = TPO_KTILE;  // targets per shared-memory tile
 constexpr int KDMAX = 8;
 
 template <typename T>
@@ -115,7 +120,9 @@ __global__ void __launch_bounds__(KW * 32)
   using A = KnnArith<T>;
   using V = typename A::V;
   constexpr int DC = DT > 0 ? DT : KDMAX;
-  __shared__ T s_c[KTILE][DC];
+  // D=3 uses long tiles (fewer block barriers); general D keeps 256 targets
+  constexpr int TILE = DT == 3 ? KTILE : 256;
+  __shared__ T s_c[TILE][DC];
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -134,6 +141,15 @@ __global__ void __launch_bounds__(KW * 32)
     for (int d = 0; d < DC; ++d)
       q[i][d] = (qv[i] && d < Dn) ? p1[(n * P1 + q0 + i) * Dn + d] : T(0.0f);
   }
+  // fp32, D=3, squared L2: queries also kept as packed pairs {q_2i, q_2i+1}
+  constexpr bool kPacked = std::is_same<T, float>::value && DT == 3 && NORM == 2 && (KQ % 2 == 0);
+  u64 QP[kPacked ? KQ / 2 : 1][3];
+  if constexpr (kPacked) {
+#pragma unroll
+    for (int ip = 0; ip < KQ / 2; ++ip)
+#pragma unroll
+      for (int d = 0; d < 3; ++d) QP[ip][d] = pk((float)q[2 * ip][d], (float)q[2 * ip + 1][d]);
+  }
   V Ld[KQ], thr[KQ];
   int Li[KQ];
 #pragma unroll
@@ -147,8 +163,8 @@ __global__ void __launch_bounds__(KW * 32)
   const bool blk_active = blk_q0 < L1;
 
   if (blk_active) {
-    for (int64_t t0 = 0; t0 < L2; t0 += KTILE) {
-      const int nt = (int)min64(KTILE, L2 - t0);
+    for (int64_t t0 = 0; t0 < L2; t0 += TILE) {
+      const int nt = (int)min64(TILE, L2 - t0);
       __syncthreads();
       {
         const T* src = p2 + (n * P2 + t0) * Dn;
@@ -173,9 +189,26 @@ __global__ void __launch_bounds__(KW * 32)
           V dv[KQ];
           unsigned bal[KQ];
           unsigned any = 0;
+          if constexpr (kPacked) {
+            // two queries per packed fp32x2 sub/mul; the sums stay scalar .rn adds
+            // (never fused), giving ((dx*dx + dy*dy) + dz*dz) exactly
+            const u64 CX = pk(cc[0], cc[0]), CY = pk(cc[1], cc[1]), CZ = pk(cc[2], cc[2]);
+#pragma unroll
+            for (int ip = 0; ip < KQ / 2; ++ip) {
+              const u64 dx = sub2(QP[ip][0], CX), dy = sub2(QP[ip][1], CY), dz = sub2(QP[ip][2], CZ);
+              float x0, x1, y0, y1, z0, z1;
+              upk(mul2(dx, dx), x0, x1);
+              upk(mul2(dy, dy), y0, y1);
+              upk(mul2(dz, dz), z0, z1);
+              dv[2 * ip] = __fadd_rn(__fadd_rn(x0, y0), z0);
+              dv[2 * ip + 1] = __fadd_rn(__fadd_rn(x1, y1), z1);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < KQ; ++i) dv[i] = knn_dist<T, DT, NORM, MODE>(q[i], cc, Dn);
+          }
 #pragma unroll
           for (int i = 0; i < KQ; ++i) {
-            dv[i] = knn_dist<T, DT, NORM, MODE>(q[i], cc, Dn);
             bal[i] = __ballot_sync(0xffffffffu, qv[i] && cv && dv[i] < thr[i]);
             any |= bal[i];
           }
