@@ -63,7 +63,10 @@ TPO_API int tpo_abi_version(void);
  * a bulk copy into shared memory that gives up sets bit 0
  * (TPO_DEVERR_BULK_TIMEOUT) and the kernel continues.  Reads the flags into
  * *flags (synchronous) and clears them if `clear` is non-zero. */
-enum tpo_device_errors { TPO_DEVERR_BULK_TIMEOUT = 1 };
+enum tpo_device_errors {
+  TPO_DEVERR_BULK_TIMEOUT = 1, /* a bulk copy's mbarrier wait gave up           */
+  TPO_DEVERR_GRID_TIMEOUT = 2  /* fps: a grid-wide step barrier wait gave up     */
+};
 TPO_API int tpo_device_error_flags(unsigned* flags, int clear);
 
 /* ------------------------------------------------------------------------- */
@@ -193,6 +196,31 @@ TPO_API int tpo_knn_gather_fwd(int dtype, const void* x, const int64_t* idx, con
 TPO_API int tpo_knn_gather_bwd(int dtype, const void* grad_out, const int64_t* idx,
                        const int64_t* lengths, int64_t N, int64_t M, int64_t U, int64_t L,
                        int64_t K, void* grad_x, void* stream);
+
+/* ------------------------------------------------------------------------- */
+/* gather_points (the gather that follows furthest-point sampling).  Replaces
+ * gather_points_cuda_forward / _backward (torch_point_ops/fps/csrc/cuda/fps.cu:
+ * 63-97, 318-401) behind torch_point_ops_fps::gather_points_forward /
+ * gather_points_backward (fps/csrc/fps.cpp:160-161):
+ *   points (N,C,P) dtype, idx (N,M) int64, out (N,C,M): out[n,c,j] = points[n,c,idx[n,j]]
+ * Indices outside [0,P) give 0 (the reference does not check them).  The
+ * backward fully writes grad_points (N,C,P) with the scatter-add of grad_out. */
+/* Furthest point sampling.  Replaces fps_cuda_forward (torch_point_ops/fps/csrc/
+ * cuda/fps.cu:261-316, kernel :108-213) behind torch_point_ops_fps::fps_forward
+ * (fps/csrc/fps.cpp:159):
+ *   points (B,P,3) dtype, idx (B,S) int64; 0 < S <= P (else TPO_ERR_INVALID_ARGUMENT).
+ * Same indices as the reference CUDA kernel, ties included (see fps.cu here).
+ * Clouds larger than the GPU's register file can hold (about 4.7M fp32 points)
+ * return TPO_ERR_UNSUPPORTED.  Large clouds run as a cooperative grid that
+ * needs tpo_fps_workspace_size() bytes of workspace (0 otherwise). */
+TPO_API size_t tpo_fps_workspace_size(int dtype, int64_t B, int64_t P);
+TPO_API int tpo_fps_fwd(int dtype, const void* points, int64_t B, int64_t P, int64_t S,
+                        int64_t* idx, void* workspace, size_t workspace_bytes, void* stream);
+
+TPO_API int tpo_gather_points_fwd(int dtype, const void* points, const int64_t* idx, int64_t N,
+                                  int64_t C, int64_t P, int64_t M, void* out, void* stream);
+TPO_API int tpo_gather_points_bwd(int dtype, const void* grad_out, const int64_t* idx, int64_t N,
+                                  int64_t C, int64_t P, int64_t M, void* grad_points, void* stream);
 
 #ifdef __cplusplus
 }

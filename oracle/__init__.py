@@ -144,6 +144,42 @@ def knn_gather(x, idx, lengths=None):
     return out
 
 
+def fps(points, nsamples: int):
+    """Reference CUDA furthest_point_sampling semantics: (B,P,3) -> (B,nsamples) int64."""
+    points = _c(points)
+    B, P, _ = points.shape
+    idx = np.zeros((B, nsamples), np.int64)
+    fn = getattr(lib(), "oracle_fps_" + _SUFFIX[points.dtype])
+    I = ctypes.c_int64
+    fn(I(B), I(P), I(nsamples), _p(points), _p(idx))
+    return idx
+
+
+def gather_points(points, idx):
+    """out[b,c,j] = points[b,c,idx[b,j]]: (B,C,P), (B,S) -> (B,C,S)."""
+    points = _c(points)
+    idx = _c(idx, np.int64)
+    B, C, P = points.shape
+    S = idx.shape[1]
+    out = np.zeros((B, C, S), points.dtype)
+    fn = getattr(lib(), "oracle_gather_points_" + _SUFFIX[points.dtype])
+    I = ctypes.c_int64
+    fn(I(B), I(C), I(P), I(S), _p(points), _p(idx), _p(out))
+    return out
+
+
+def gather_points_bwd(grad_out, idx, P: int):
+    """Scatter-add of grad_out (B,C,S) into (B,C,P), in (b, c, j) order."""
+    go = _c(grad_out)
+    idx = _c(idx, np.int64)
+    B, C, S = go.shape
+    gp = np.zeros((B, C, P), go.dtype)
+    fn = getattr(lib(), "oracle_gather_points_bwd_" + _SUFFIX[go.dtype])
+    I = ctypes.c_int64
+    fn(I(B), I(C), I(P), I(S), _p(go), _p(idx), _p(gp))
+    return gp
+
+
 # ---------------- the unmodified reference, built by oracle/Makefile.ref ----------------
 _ref_loaded = {}
 
@@ -179,3 +215,13 @@ def ref_chamfer():
     if _load_ref("chamfer_cuda_ref.so") is None:
         return None
     return torch.ops.torch_point_ops_chamfer
+
+
+def ref_fps():
+    """Reference fps op library (CPU and CUDA kernels of torch_point_ops.fps).
+    Returns torch.ops.torch_point_ops_fps or None."""
+    import torch
+
+    if _load_ref("fps_cuda_ref.so") is None:
+        return None
+    return torch.ops.torch_point_ops_fps

@@ -25,6 +25,25 @@
  *               with the L1 sign at equality taken from the CUDA kernel
  *               (knn.cu:447-449: 0 when p1 == p2) when l1_zero_at_tie != 0.
  *
+ *   fps         furthest_point_sampling_kernel, torch_point_ops/fps/csrc/cuda/fps.cu:108-213
+ *               with its launch at :215-316 (the CUDA semantics, not the CPU
+ *               path of fps/csrc/fps.cpp:17-88, which differs: it masks selected
+ *               points and lets degenerate points win).  idx[0] = 0; temp starts
+ *               at 1e10 (1e4 for fp16, :291); a point with |p|^2 <= 1e-3 is never
+ *               updated nor chosen (:139-140); d = |p - p_old|^2 with the fma
+ *               contraction below (:142), temp = min(d, temp) (:143); the argmax
+ *               ties resolve as the reference's block reduction does: thread
+ *               t = k mod bs keeps its first maximum in k order (strict '>',
+ *               :145-146), and the halving tree (:152-205, __update :99-106)
+ *               merges slot i with i+s for s = bs/2 .. 1 keeping slot i on ties,
+ *               so bit 0 of the winning thread is decided last: among equal
+ *               maxima the point with the smallest (bitreverse(k mod bs), k)
+ *               wins, bs = min(512, 2^floor(log2 P)) (opt_n_threads,
+ *               fps.cu:56-59).  If no point is valid the answer is 0 (besti's
+ *               initial value, :131).
+ *   gather_points gather_points_kernel / _grad_kernel, fps.cu:63-97
+ *               (out[n,c,j] = points[n,c,idx[n,j]]; backward scatter-adds).
+ *
  * Rounding modes (`mode`):
  *   0  "exact": every product and sum rounded separately, no contraction.
  *      This is the reference CPU path (g++ -O3 on x86-64 baseline emits no FMA).
@@ -287,3 +306,92 @@ void oracle_knn_bwd_f16(int64_t Nb, int64_t P1, int64_t P2, int64_t D, const h16
   KBWD_BODY(h16, hr((float)hr((float)g * 2.0f) * (float)hr((float)x - (float)y)),
             SIGNV(h16, x, y, g), ACC_H)
 }
+
+/* ---------------- furthest point sampling (reference CUDA semantics) ---------------- */
+static int64_t fps_block_size(int64_t P) {
+  int64_t bs = 1;
+  while (bs * 2 <= P && bs < 512) bs *= 2;
+  return bs;
+}
+static int64_t bitrev(int64_t c, int64_t bs) {
+  int64_t r = 0;
+  for (int64_t b = 1; b < bs; b <<= 1) r = (r << 1) | ((c & b) ? 1 : 0);
+  return r;
+}
+/* Visit order of the reference's tie resolution: (bitreverse(k mod bs), k). */
+#define FPS_BODY(T, LARGE, MAG, DIST, VALID)                                   \
+  const int64_t bs = fps_block_size(P);                                        \
+  T* temp = (T*)malloc(sizeof(T) * (P > 0 ? P : 1));                           \
+  for (int64_t b = 0; b < B; ++b) {                                            \
+    const T* pts = points + b * P * 3;                                         \
+    int64_t* out = idx + b * S;                                                \
+    if (S <= 0) continue;                                                      \
+    for (int64_t k = 0; k < P; ++k) temp[k] = (T)(LARGE);                      \
+    int64_t old = 0;                                                           \
+    out[0] = 0;                                                                \
+    for (int64_t j = 1; j < S; ++j) {                                          \
+      const T x1 = pts[old * 3], y1 = pts[old * 3 + 1], z1 = pts[old * 3 + 2]; \
+      T best = (T)(-1.0f);                                                     \
+      int64_t besti = 0;                                                       \
+      int have = 0;                                                            \
+      for (int64_t c = 0; c < bs; ++c)                                         \
+        for (int64_t k = bitrev(c, bs); k < P; k += bs) {                      \
+          const T x2 = pts[k * 3], y2 = pts[k * 3 + 1], z2 = pts[k * 3 + 2];   \
+          const T mag = MAG;                                                   \
+          if (!(VALID)) continue;                                              \
+          const T d = DIST;                                                    \
+          const T d2 = (d < temp[k]) ? d : temp[k];                            \
+          temp[k] = d2;                                                        \
+          if (!have || d2 > best) { best = d2; besti = k; have = 1; }          \
+        }                                                                      \
+      old = have ? besti : 0;                                                  \
+      out[j] = old;                                                            \
+    }                                                                          \
+  }                                                                            \
+  free(temp);
+
+void oracle_fps_f32(int64_t B, int64_t P, int64_t S, const float* points, int64_t* idx) {
+  FPS_BODY(float, 1e10f, fmaf(z2, z2, fmaf(x2, x2, y2 * y2)),
+           d2_f32(1, x2 - x1, y2 - y1, z2 - z1), mag > 1e-3f)
+}
+void oracle_fps_f64(int64_t B, int64_t P, int64_t S, const double* points, int64_t* idx) {
+  FPS_BODY(double, 1e10, fma(z2, z2, fma(x2, x2, y2 * y2)),
+           d2_f64(1, x2 - x1, y2 - y1, z2 - z1), mag > 1e-3)
+}
+void oracle_fps_f16(int64_t B, int64_t P, int64_t S, const h16* points, int64_t* idx) {
+  const float thr = (float)(h16)1e-3f;
+  FPS_BODY(h16, 1e4f,
+           hr((float)hr((float)hr((float)x2 * (float)x2) + (float)hr((float)y2 * (float)y2)) +
+              (float)hr((float)z2 * (float)z2)),
+           d2_f16(hr((float)x2 - (float)x1), hr((float)y2 - (float)y1), hr((float)z2 - (float)z1)),
+           (float)mag > thr)
+}
+
+/* gather_points: out (B,C,S) = points (B,C,P) at idx (B,S); backward scatter-add. */
+#define GP_FWD(T)                                                              \
+  for (int64_t b = 0; b < B; ++b)                                              \
+    for (int64_t c = 0; c < C; ++c)                                            \
+      for (int64_t j = 0; j < S; ++j)                                          \
+        out[(b * C + c) * S + j] = points[(b * C + c) * P + idx[b * S + j]];
+#define GP_BWD(T, ADD)                                                         \
+  memset(gp, 0, sizeof(T) * B * C * P);                                        \
+  for (int64_t b = 0; b < B; ++b)                                              \
+    for (int64_t c = 0; c < C; ++c)                                            \
+      for (int64_t j = 0; j < S; ++j) {                                        \
+        T* dst = gp + (b * C + c) * P + idx[b * S + j];                        \
+        *dst = ADD(*dst, go[(b * C + c) * S + j]);                             \
+      }
+#define ADD_PLAIN(a, v) ((a) + (v))
+#define ADD_HALF(a, v) hr((float)(a) + (float)(v))
+void oracle_gather_points_f32(int64_t B, int64_t C, int64_t P, int64_t S, const float* points,
+                              const int64_t* idx, float* out) { GP_FWD(float) }
+void oracle_gather_points_f64(int64_t B, int64_t C, int64_t P, int64_t S, const double* points,
+                              const int64_t* idx, double* out) { GP_FWD(double) }
+void oracle_gather_points_f16(int64_t B, int64_t C, int64_t P, int64_t S, const h16* points,
+                              const int64_t* idx, h16* out) { GP_FWD(h16) }
+void oracle_gather_points_bwd_f32(int64_t B, int64_t C, int64_t P, int64_t S, const float* go,
+                                  const int64_t* idx, float* gp) { GP_BWD(float, ADD_PLAIN) }
+void oracle_gather_points_bwd_f64(int64_t B, int64_t C, int64_t P, int64_t S, const double* go,
+                                  const int64_t* idx, double* gp) { GP_BWD(double, ADD_PLAIN) }
+void oracle_gather_points_bwd_f16(int64_t B, int64_t C, int64_t P, int64_t S, const h16* go,
+                                  const int64_t* idx, h16* gp) { GP_BWD(h16, ADD_HALF) }

@@ -134,3 +134,32 @@ def chamfer_loss_bwd(x1, x2, state, grad_loss, reduction=0, flags=0):
                                      ctypes.c_int(reduction), p(state), p(grad_loss), p(gx1),
                                      p(gx2), stream()))
     return gx1, gx2
+
+
+def fps_fwd(points, S):
+    B, P, _ = points.shape
+    dt = DT[points.dtype]
+    idx = torch.empty(B, S, dtype=torch.int64, device=points.device)
+    lib().tpo_fps_workspace_size.restype = ctypes.c_size_t
+    ws_n = lib().tpo_fps_workspace_size(dt, I64(B), I64(P))
+    ws = torch.empty(max(ws_n, 1), dtype=torch.uint8, device=points.device)
+    check(lib().tpo_fps_fwd(dt, p(points), I64(B), I64(P), I64(S), p(idx), p(ws),
+                            ctypes.c_size_t(ws_n), stream()))
+    return idx
+
+
+def gather_points_fwd(points, idx):
+    B, Cc, P = points.shape
+    S = idx.shape[1]
+    out = torch.empty(B, Cc, S, dtype=points.dtype, device=points.device)
+    check(lib().tpo_gather_points_fwd(DT[points.dtype], p(points), p(idx), I64(B), I64(Cc), I64(P),
+                                      I64(S), p(out), stream()))
+    return out
+
+
+def gather_points_bwd(gout, idx, P):
+    B, Cc, S = gout.shape
+    gp = torch.empty(B, Cc, P, dtype=gout.dtype, device=gout.device)
+    check(lib().tpo_gather_points_bwd(DT[gout.dtype], p(gout), p(idx), I64(B), I64(Cc), I64(P),
+                                      I64(S), p(gp), stream()))
+    return gp

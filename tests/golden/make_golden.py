@@ -6,7 +6,12 @@ knn.cpp) and records its outputs on seeded inputs.  The reference's CPU path is
 the only one runnable without a GPU; chamfer's CPU path is knn(K=1) in both
 directions + knn_backward (chamfer itself raises on CPU, chamfer.cpp:21-24).
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py [chamfer_knn|fps|all]
+
+fps: the reference's CPU fps_forward / gather_points_forward / _backward
+(torch_point_ops/fps/csrc/fps.cpp:17-145) on clouds without degenerate points
+(|p|^2 > 1e-3) and without exact ties, where its CPU path and its CUDA kernel
+(which the oracle restates) select the same points.
 """
 import os
 import subprocess
@@ -67,5 +72,35 @@ def main():
     print("wrote", sorted(os.listdir(HERE)))
 
 
+def fps_main():
+    import oracle
+
+    if oracle.ref_fps() is None:
+        subprocess.check_call(["make", "-f", os.path.join(ROOT, "oracle", "Makefile.ref"), "cuda"])
+    ops = oracle.ref_fps()
+    assert ops is not None, "reference fps library not available"
+    g = torch.Generator().manual_seed(4321)
+    dts = {"f32": torch.float32, "f64": torch.float64, "f16": torch.float16}
+    for name, dt in dts.items():
+        out = {}
+        for ci, (B, P, S) in enumerate([(2, 50, 12), (3, 333, 40), (1, 1200, 64)]):
+            x = torch.randn(B, P, 3, generator=g)
+            x = torch.where(x.pow(2).sum(-1, keepdim=True) < 0.01, x + 0.5, x).to(dt)
+            out[f"points{ci}"] = x.numpy()
+            out[f"idx{ci}"] = ops.fps_forward(x, S).numpy()
+        pts = torch.randn(2, 5, 90, generator=g).to(dt)
+        gidx = torch.stack([torch.randperm(90, generator=g)[:31] for _ in range(2)])
+        gout = torch.randn(2, 5, 31, generator=g).to(dt)
+        out.update(gp_points=pts.numpy(), gp_idx=gidx.numpy(),
+                   gp_out=ops.gather_points_forward(pts, gidx).numpy(), gp_grad_out=gout.numpy(),
+                   gp_grad_points=ops.gather_points_backward(gout, gidx, 90).numpy())
+        np.savez_compressed(os.path.join(HERE, f"fps_{name}.npz"), **out)
+    print("wrote", sorted(os.listdir(HERE)))
+
+
 if __name__ == "__main__":
-    main()
+    what = sys.argv[1] if len(sys.argv) > 1 else "all"
+    if what in ("chamfer_knn", "all"):
+        main()
+    if what in ("fps", "all"):
+        fps_main()

@@ -1,0 +1,158 @@
+"""Furthest point sampling and gather_points on the B200 against the CPU oracle
+(a restatement of the reference CUDA kernels, torch_point_ops/fps/csrc/cuda/
+fps.cu), through the C ABI and the torch API.  FPS indices are bit-exact; the
+cases cover every group shape the planner picks (one CTA, a thread-block
+cluster, a cooperative grid), ties, degenerate points and ragged sizes."""
+import numpy as np
+import pytest
+import torch
+
+import capi_util as C
+import oracle
+import torch_point_ops_b200 as tpo
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _cloud(B, P, dtype, seed, kind="normal"):
+    g = torch.Generator().manual_seed(seed)
+    if kind == "normal":
+        x = torch.randn(B, P, 3, generator=g)
+    elif kind == "lattice":  # integer grid: many exactly equal distances
+        x = torch.randint(-4, 5, (B, P, 3), generator=g).float()
+    elif kind == "degenerate":  # a third of the points inside |p|^2 <= 1e-3
+        x = torch.randn(B, P, 3, generator=g)
+        x[:, ::3] *= 1e-3
+    elif kind == "duplicates":
+        x = torch.randn(B, P, 3, generator=g)
+        x[:, P // 2:] = x[:, : P - P // 2]
+    return x.to(dtype)
+
+
+CASES = [
+    (3, 100, 20, "normal"),
+    (2, 1000, 64, "normal"),
+    (4, 37, 37, "normal"),       # nsamples == P
+    (1, 1, 1, "normal"),
+    (2, 513, 100, "lattice"),    # bs = 512, P not a multiple of it
+    (2, 300, 300, "lattice"),    # bs = 256; runs out of distinct points
+    (2, 2000, 200, "degenerate"),
+    (2, 700, 400, "duplicates"),
+    (2, 16384, 300, "normal"),   # cluster of CTAs
+    (1, 20000, 200, "lattice"),
+    (8, 4096, 128, "normal"),
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.float64])
+@pytest.mark.parametrize("B,P,S,kind", CASES)
+def test_fps_matches_oracle(B, P, S, kind, dtype):
+    x = _cloud(B, P, dtype, seed=P + S, kind=kind)
+    idx = C.fps_fwd(x.to(DEV), S)
+    torch.cuda.synchronize()
+    ref = oracle.fps(x.numpy(), S)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16])
+def test_fps_all_degenerate(dtype):
+    x = torch.zeros(2, 50, 3, dtype=dtype)
+    idx = tpo.furthest_point_sampling(x.to(DEV), 10)
+    assert torch.equal(idx.cpu(), torch.zeros(2, 10, dtype=torch.int64))
+    np.testing.assert_array_equal(idx.cpu().numpy(), oracle.fps(x.numpy(), 10))
+
+
+@pytest.mark.parametrize("P,S", [(200_000, 48), (600_000, 24)])
+def test_fps_large_cloud_grid(P, S):
+    """Clouds beyond one cluster's registers run as a cooperative grid."""
+    x = _cloud(1, P, torch.float32, seed=7, kind="normal")
+    idx = C.fps_fwd(x.to(DEV), S)
+    np.testing.assert_array_equal(idx.cpu().numpy(), oracle.fps(x.numpy(), S))
+    flags = ctypes_flags()
+    assert flags == 0
+
+
+def ctypes_flags():
+    import ctypes
+
+    f = ctypes.c_uint(0)
+    C.check(C.lib().tpo_device_error_flags(ctypes.byref(f), 1))
+    return f.value
+
+
+def test_fps_torch_api_and_errors():
+    x = _cloud(2, 500, torch.float32, seed=3).to(DEV)
+    idx = tpo.furthest_point_sampling(x, 32)
+    assert idx.dtype == torch.int64 and idx.shape == (2, 32)
+    assert torch.all(idx[:, 0] == 0)
+    for n in range(2):
+        assert len(torch.unique(idx[n])) == 32
+    with pytest.raises(ValueError):
+        tpo.furthest_point_sampling(x[0], 5)
+    with pytest.raises(ValueError):
+        tpo.furthest_point_sampling(x[..., :2], 5)
+    with pytest.raises(ValueError):
+        tpo.furthest_point_sampling(x, 0)
+    with pytest.raises(ValueError):
+        tpo.furthest_point_sampling(x, 501)
+    # C ABI rejects the same
+    import ctypes
+
+    out = torch.empty(2, 600, dtype=torch.int64, device=DEV)
+    rc = C.lib().tpo_fps_fwd(0, C.p(x), C.I64(2), C.I64(500), C.I64(600), C.p(out), C.VP(0),
+                             ctypes.c_size_t(0), C.stream())
+    assert rc == 1
+
+
+def test_fps_modules():
+    x = _cloud(2, 400, torch.float32, seed=4).to(DEV)
+    m = tpo.FarthestPointSampling(16, return_gathered=True)
+    idx, pts = m(x)
+    assert torch.equal(pts, torch.stack([x[n, idx[n]] for n in range(2)]))
+    idx2, pts2 = tpo.farthest_point_sample_and_gather(x, 16)
+    assert torch.equal(idx, idx2) and torch.equal(pts, pts2)
+    assert torch.equal(tpo.FPSFunction()(x, 16), idx)
+    with pytest.raises(ValueError):
+        tpo.FarthestPointSampling(0)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.float64])
+def test_gather_points_fwd_bwd(dtype):
+    g = torch.Generator().manual_seed(11)
+    B, Cc, P, S = 3, 6, 500, 77
+    pts = torch.randn(B, Cc, P, generator=g).to(dtype)
+    idx = torch.stack([torch.randperm(P, generator=g)[:S] for _ in range(B)])
+    idx[:, 5] = idx[:, 9]  # repeated index: the backward must accumulate
+    out = C.gather_points_fwd(pts.to(DEV), idx.to(DEV))
+    np.testing.assert_array_equal(out.cpu().numpy(), oracle.gather_points(pts.numpy(), idx.numpy()))
+    go = torch.randn(B, Cc, S, generator=g).to(dtype)
+    gp = C.gather_points_bwd(go.to(DEV), idx.to(DEV), P)
+    ref = oracle.gather_points_bwd(go.numpy(), idx.numpy(), P)
+    # at most two terms meet in one slot here: the sum is order-independent
+    np.testing.assert_array_equal(gp.cpu().numpy(), ref)
+
+
+def test_gather_points_autograd_and_errors():
+    g = torch.Generator().manual_seed(12)
+    pts = torch.randn(2, 4, 100, generator=g, dtype=torch.float64).to(DEV).requires_grad_()
+    idx = torch.randint(0, 100, (2, 30), generator=g).to(DEV)
+    out = tpo.gather_points(pts, idx)
+    ref = torch.gather(pts, 2, idx[:, None, :].expand(-1, 4, -1))
+    assert torch.equal(out, ref)
+    w = torch.randn_like(out)
+    (gp,) = torch.autograd.grad((out * w).sum(), pts)
+    (gr,) = torch.autograd.grad((ref * w).sum(), pts)
+    torch.testing.assert_close(gp, gr, rtol=0, atol=1e-12)
+    assert torch.autograd.gradcheck(lambda p: tpo.gather_points(p, idx), (pts,))
+    gath = tpo.PointGatherer()(pts, idx)
+    assert torch.equal(gath, out)
+    with pytest.raises(ValueError):
+        tpo.gather_points(pts[0], idx)
+    with pytest.raises(ValueError):
+        tpo.gather_points(pts, idx[..., None])
+    with pytest.raises(ValueError):
+        tpo.gather_points(pts, idx[:1])
+    # empty gathers
+    e = tpo.gather_points(pts, idx[:, :0])
+    assert e.shape == (2, 4, 0)

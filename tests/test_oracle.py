@@ -104,3 +104,29 @@ def test_oracle_vs_reference_live():
         oi, od = oracle.knn_fwd(p1.numpy(), p2.numpy(), l1.numpy(), l2.numpy(), 2, 12, 0)
         assert np.array_equal(i.numpy(), oi)
         assert np.array_equal(_bits(d.numpy()), _bits(od))
+
+
+@pytest.mark.parametrize("path", sorted(glob.glob(os.path.join(GOLD, "fps_*.npz"))))
+def test_oracle_fps_golden(path):
+    """FPS indices and gather_points values recorded from the reference's CPU ops."""
+    z = np.load(path)
+    for ci in range(3):
+        x, ref = z[f"points{ci}"], z[f"idx{ci}"]
+        assert np.array_equal(oracle.fps(x, ref.shape[1]), ref)
+    assert np.array_equal(oracle.gather_points(z["gp_points"], z["gp_idx"]), z["gp_out"])
+    assert np.array_equal(oracle.gather_points_bwd(z["gp_grad_out"], z["gp_idx"], 90), z["gp_grad_points"])
+
+
+def test_oracle_fps_tie_order():
+    """Equal maxima resolve like the reference CUDA kernel's halving reduction:
+    smallest bit-reversed thread (k mod bs), then smallest k.  P = 6 gives bs = 4,
+    threads in tie order 0 (points 0, 4), 2 (point 2), 1 (points 1, 5), 3.
+    Points 1..5 are all at squared distance 2 from point 0, so step 1 picks 4
+    (thread 0); every remaining point is then still at 2, and step 2 picks 2
+    (thread 2 ranks before thread 1) -- neither the lowest index nor the lowest
+    thread.  (This order reproduces the reference's CUDA output on lattice
+    clouds; tests/test_ref_cuda_pin.py checks it on the GPU.)"""
+    x = np.array([[[1, 0, 0], [0, 1, 0], [0, -1, 0], [0, 0, 1], [0, 0, -1], [1, 1, 1]]],
+                 np.float32)
+    for dt in (np.float32, np.float64, np.float16):
+        assert oracle.fps(x.astype(dt), 3).tolist() == [[0, 4, 2]]

@@ -58,3 +58,43 @@ def test_reference_knn_cuda_rounding(dtype):
     assert np.array_equal(ri.cpu().numpy(), oi)
     i, d = C.knn_fwd(p1.cuda(), p2.cuda(), L1.cuda(), L2.cuda(), 2, 16, 0)
     assert torch.equal(i.cpu(), ri.cpu())
+
+
+FPS_PIN_CASES = [(2, 1000, 64, 0), (2, 300, 300, 1), (1, 5000, 200, 2), (2, 2048, 128, 3),
+                 (3, 777, 100, 4)]
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float64, torch.float16])
+@pytest.mark.parametrize("B,P,S,kind", FPS_PIN_CASES)
+def test_reference_fps_cuda(B, P, S, kind, dtype):
+    """The reference CUDA FPS kernel, the oracle and this library agree index for
+    index -- lattice clouds (kind 1, 3) force ties, kind 2 has degenerate points,
+    kind 4 duplicates."""
+    ops = oracle.ref_fps()
+    if ops is None:
+        pytest.skip("reference fps build not present in oracle/_ref")
+    g = torch.Generator().manual_seed(P + kind)
+    if kind in (1, 3):
+        x = torch.randint(-3, 4, (B, P, 3), generator=g).float()
+    else:
+        x = torch.randn(B, P, 3, generator=g)
+        if kind == 2:
+            x[:, 1::4] *= 1e-2
+        if kind == 4:
+            x[:, P // 2:] = x[:, : P - P // 2]
+    x = x.to(dtype)
+    ri = ops.fps_forward(x.cuda(), S).cpu()
+    np.testing.assert_array_equal(ri.numpy(), oracle.fps(x.numpy(), S))
+    mine = C.fps_fwd(x.cuda(), S).cpu()
+    assert torch.equal(mine, ri)
+
+
+def test_reference_gather_points_cuda():
+    ops = oracle.ref_fps()
+    if ops is None:
+        pytest.skip("reference fps build not present in oracle/_ref")
+    g = torch.Generator().manual_seed(5)
+    pts = torch.randn(2, 5, 300, generator=g)
+    idx = torch.randint(0, 300, (2, 64), generator=g)
+    ref = ops.gather_points_forward(pts.cuda(), idx.cuda()).cpu()
+    assert torch.equal(C.gather_points_fwd(pts.cuda(), idx.cuda()).cpu(), ref)

@@ -20,6 +20,7 @@ if not (os.path.exists(CAPI_PATH) and os.path.exists(TORCH_BINDING_PATH)):
 torch.ops.load_library(TORCH_BINDING_PATH)
 chamfer_ops = torch.ops.torch_point_ops_b200_chamfer
 knn_ops = torch.ops.torch_point_ops_b200_knn
+fps_ops = torch.ops.torch_point_ops_b200_fps
 
 _capi = None
 

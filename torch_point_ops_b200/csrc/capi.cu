@@ -49,7 +49,11 @@ const char* tpo_status_string(int status) {
 
 int tpo_device_error_flags(unsigned* flags, int clear) {
   if (!flags) return fail(TPO_ERR_INVALID_ARGUMENT, "device_error_flags: null output");
-  return device_error_flags(flags, clear != 0);
+  unsigned a = 0, b = 0;
+  int s = device_error_flags(&a, clear != 0);
+  if (!s) s = fps_device_error_flags(&b, clear != 0);
+  *flags = a | b;
+  return s;
 }
 
 int tpo_chamfer_key_bytes(int dtype) {
@@ -323,6 +327,43 @@ int tpo_knn_gather_bwd(int dtype, const void* grad_out, const int64_t* idx, cons
       (s = cuda_status(cudaMemsetAsync(grad_x, 0, (size_t)dtype_size(dtype) * N * M * U, st))))
     return s;
   return knn_gather_backward(dtype, grad_out, idx, lengths, N, M, U, L, K, grad_x, st);
+}
+
+size_t tpo_fps_workspace_size(int dtype, int64_t B, int64_t P) {
+  if (!valid_dtype(dtype) || B < 0 || P <= 0) return 0;
+  return fps_workspace_size(dtype, B, P);
+}
+
+int tpo_fps_fwd(int dtype, const void* points, int64_t B, int64_t P, int64_t S, int64_t* idx,
+                void* workspace, size_t workspace_bytes, void* stream) {
+  if (!valid_dtype(dtype)) return fail(TPO_ERR_INVALID_ARGUMENT, "fps: dtype must be f32, f16 or f64");
+  if (B < 0 || P < 0 || P > INT32_MAX) return fail(TPO_ERR_INVALID_ARGUMENT, "fps: bad shape");
+  if (S <= 0) return fail(TPO_ERR_INVALID_ARGUMENT, "fps: nsamples must be positive");
+  if (S > P) return fail(TPO_ERR_INVALID_ARGUMENT, "fps: nsamples cannot exceed number of points");
+  if (B > 0 && (!points || !idx)) return fail(TPO_ERR_INVALID_ARGUMENT, "fps: null pointer");
+  return fps_forward(dtype, points, B, P, S, idx, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+int tpo_gather_points_fwd(int dtype, const void* points, const int64_t* idx, int64_t N, int64_t C,
+                          int64_t P, int64_t M, void* out, void* stream) {
+  if (!valid_dtype(dtype)) return fail(TPO_ERR_INVALID_ARGUMENT, "gather_points: bad dtype");
+  if (N < 0 || C < 0 || P < 0 || M < 0) return fail(TPO_ERR_INVALID_ARGUMENT, "gather_points: bad shape");
+  if (N * C * M > 0 && (!points || !idx || !out)) return fail(TPO_ERR_INVALID_ARGUMENT, "gather_points: null pointer");
+  return gather_points_forward(dtype, points, idx, N, C, P, M, out, (cudaStream_t)stream);
+}
+
+int tpo_gather_points_bwd(int dtype, const void* grad_out, const int64_t* idx, int64_t N, int64_t C,
+                          int64_t P, int64_t M, void* grad_points, void* stream) {
+  if (!valid_dtype(dtype)) return fail(TPO_ERR_INVALID_ARGUMENT, "gather_points_bwd: bad dtype");
+  if (N < 0 || C < 0 || P < 0 || M < 0) return fail(TPO_ERR_INVALID_ARGUMENT, "gather_points_bwd: bad shape");
+  if ((N * C * P > 0 && !grad_points) || (N * C * M > 0 && (!grad_out || !idx)))
+    return fail(TPO_ERR_INVALID_ARGUMENT, "gather_points_bwd: null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  int s;
+  if (N * C * P > 0 &&
+      (s = cuda_status(cudaMemsetAsync(grad_points, 0, (size_t)dtype_size(dtype) * N * C * P, st))))
+    return s;
+  return gather_points_backward(dtype, grad_out, idx, N, C, P, M, grad_points, st);
 }
 
 }  // extern "C"

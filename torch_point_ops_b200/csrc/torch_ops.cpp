@@ -3,8 +3,11 @@
 // Same schemas as the reference's operator libraries
 //   torch_point_ops_chamfer  (torch_point_ops/chamfer/csrc/chamfer.cpp:34-39)
 //   torch_point_ops_knn      (torch_point_ops/knn/csrc/knn.cpp:167-172)
+//   torch_point_ops_fps      (torch_point_ops/fps/csrc/fps.cpp:158-162; fps_forward,
+//                             gather_points_forward / _backward)
 // registered under the namespaces torch_point_ops_b200_chamfer /
-// torch_point_ops_b200_knn so both libraries can live in one process.  Extra ops:
+// torch_point_ops_b200_knn / torch_point_ops_b200_fps so both libraries can live
+// in one process.  Extra ops:
 // *_ex variants taking the rounding flags, the row-sharded split of the chamfer
 // forward, and knn_gather forward/backward (a torch expand+gather in the
 // reference, knn/__init__.py:136-183).  Only CUDA implementations are
@@ -324,7 +327,75 @@ at::Tensor knn_gather_backward(const at::Tensor& grad_out_, const at::Tensor& id
   return gx;
 }
 
+// fps_forward: points (N,P,3) -> idx (N,nsamples) int64.  Mirrors fps_cuda_forward
+// (torch_point_ops/fps/csrc/cuda/fps.cu:273-316) and its checks.
+at::Tensor fps_forward(const at::Tensor& points_, int64_t nsamples) {
+  TORCH_CHECK(points_.is_cuda(), "fps: points must be a CUDA tensor");
+  TORCH_CHECK(points_.dim() == 3, "fps: points must be (N, P, 3)");
+  TORCH_CHECK(points_.size(2) == 3, "FPS only supports 3D points, but got dimension ", points_.size(2));
+  TORCH_CHECK(nsamples > 0, "nsamples must be positive, but got ", nsamples);
+  TORCH_CHECK(nsamples <= points_.size(1), "nsamples (", nsamples,
+              ") cannot exceed number of points (", points_.size(1), ")");
+  const c10::cuda::CUDAGuard g(points_.device());
+  const at::Tensor pts = points_.contiguous();
+  const int64_t N = pts.size(0), P = pts.size(1);
+  auto idx = at::empty({N, nsamples}, pts.options().dtype(at::kLong));
+  const int dt = to_dtype(pts);
+  const size_t wsb = tpo_fps_workspace_size(dt, N, P);
+  at::Tensor ws;
+  if (wsb) ws = at::empty({(int64_t)wsb}, pts.options().dtype(at::kByte));
+  ok(tpo_fps_fwd(dt, pts.data_ptr(), N, P, nsamples, idx.data_ptr<int64_t>(),
+                 wsb ? ws.data_ptr() : nullptr, wsb, stream_of(pts)),
+     "fps_forward");
+  return idx;
+}
+
+// gather_points: points (N,C,P), idx (N,M) int64 -> (N,C,M).  Mirrors
+// gather_points_cuda_forward / _backward (torch_point_ops/fps/csrc/cuda/fps.cu:318-401).
+at::Tensor gather_points_forward(const at::Tensor& points_, const at::Tensor& idx_) {
+  TORCH_CHECK(points_.is_cuda() && idx_.device() == points_.device(),
+              "points and idx must be on the same CUDA device");
+  TORCH_CHECK(points_.dim() == 3 && idx_.dim() == 2 && idx_.size(0) == points_.size(0),
+              "gather_points: points must be (N, C, P) and idx (N, M)");
+  const c10::cuda::CUDAGuard g(points_.device());
+  const at::Tensor pts = points_.contiguous(), idx = idx_.to(at::kLong).contiguous();
+  const int64_t N = pts.size(0), C = pts.size(1), P = pts.size(2), M = idx.size(1);
+  auto out = at::empty({N, C, M}, pts.options());
+  ok(tpo_gather_points_fwd(to_dtype(pts), pts.data_ptr(), idx.data_ptr<int64_t>(), N, C, P, M,
+                           out.data_ptr(), stream_of(pts)),
+     "gather_points_forward");
+  return out;
+}
+
+at::Tensor gather_points_backward(const at::Tensor& grad_out_, const at::Tensor& idx_, int64_t n) {
+  TORCH_CHECK(grad_out_.is_cuda() && idx_.device() == grad_out_.device(),
+              "grad_out and idx must be on the same CUDA device");
+  TORCH_CHECK(grad_out_.dim() == 3 && idx_.dim() == 2 && idx_.size(0) == grad_out_.size(0) &&
+                  idx_.size(1) == grad_out_.size(2) && n >= 0,
+              "gather_points_backward: grad_out must be (N, C, M), idx (N, M), n >= 0");
+  const c10::cuda::CUDAGuard g(grad_out_.device());
+  const at::Tensor go = grad_out_.contiguous(), idx = idx_.to(at::kLong).contiguous();
+  const int64_t N = go.size(0), C = go.size(1), M = go.size(2);
+  auto gp = at::empty({N, C, n}, go.options());
+  ok(tpo_gather_points_bwd(to_dtype(go), go.data_ptr(), idx.data_ptr<int64_t>(), N, C, n, M,
+                           gp.data_ptr(), stream_of(go)),
+     "gather_points_backward");
+  return gp;
+}
+
 }  // namespace
+
+TORCH_LIBRARY(torch_point_ops_b200_fps, m) {
+  m.def("fps_forward(Tensor points, int nsamples) -> Tensor");
+  m.def("gather_points_forward(Tensor points, Tensor idx) -> Tensor");
+  m.def("gather_points_backward(Tensor grad_out, Tensor idx, int n) -> Tensor");
+}
+
+TORCH_LIBRARY_IMPL(torch_point_ops_b200_fps, CUDA, m) {
+  m.impl("fps_forward", &fps_forward);
+  m.impl("gather_points_forward", &gather_points_forward);
+  m.impl("gather_points_backward", &gather_points_backward);
+}
 
 TORCH_LIBRARY(torch_point_ops_b200_chamfer, m) {
   m.def("chamfer_forward(Tensor xyz1, Tensor xyz2) -> (Tensor, Tensor, Tensor, Tensor)");

@@ -2,6 +2,7 @@
 #pragma once
 
 #include <algorithm>
+#include <climits>
 #include <cstdint>
 
 #include "tpo_common.cuh"
@@ -64,6 +65,15 @@ int fill_prefetch(void* d0, size_t n0, void* d1, size_t n1, unsigned char value,
 
 // Reads (and optionally clears) the device-side error flags of this device.
 int device_error_flags(unsigned* out, bool clear);
+
+size_t fps_workspace_size(int dtype, int64_t B, int64_t P);
+int fps_forward(int dtype, const void* pts, int64_t B, int64_t P, int64_t S, int64_t* idx,
+                void* ws, size_t ws_bytes, cudaStream_t st);
+int fps_device_error_flags(unsigned* out, bool clear);
+int gather_points_forward(int dtype, const void* pts, const int64_t* idx, int64_t N, int64_t C,
+                          int64_t P, int64_t M, void* out, cudaStream_t st);
+int gather_points_backward(int dtype, const void* gout, const int64_t* idx, int64_t N, int64_t C,
+                           int64_t P, int64_t M, void* gpts, cudaStream_t st);
 
 inline int dtype_size(int dtype) {
   return dtype == TPO_F32 ? 4 : dtype == TPO_F16 ? 2 : dtype == TPO_F64 ? 8 : 0;
