@@ -48,8 +48,24 @@ def test_knn_argument_checks():
                                I64(norm), I64(K), VP(1), VP(1), VP(0))
     assert L.tpo_knn_fwd(*args(3, 1, 3)) == 1          # bad norm
     assert L.tpo_knn_fwd(*args(2, 0, 3)) == 1          # K < 1
-    assert L.tpo_knn_fwd(*args(2, 33, 3)) == 2         # K > 32: unsupported
-    assert L.tpo_knn_fwd(*args(2, 4, 9)) == 2          # D > 8: unsupported
+    assert L.tpo_knn_fwd(*args(2, 257, 3)) == 2        # K > 256: unsupported
+    assert L.tpo_knn_fwd(*args(2, 4, 0)) == 1          # D < 1
+
+
+def test_fps_argument_checks():
+    L = lib()
+    f = lambda B, P, S: L.tpo_fps_fwd(0, VP(1), I64(B), I64(P), I64(S), VP(1), VP(0),
+                                      ctypes.c_size_t(0), VP(0))
+    assert f(1, 10, 0) == 1      # nsamples must be positive
+    assert f(1, 10, 11) == 1     # nsamples > P
+    assert f(-1, 10, 5) == 1     # bad shape
+    assert L.tpo_fps_fwd(7, VP(1), I64(1), I64(10), I64(5), VP(1), VP(0), ctypes.c_size_t(0),
+                         VP(0)) == 1   # bad dtype
+    assert f(0, 10, 5) == 0      # empty batch: nothing to do
+    g = lambda N, C, P, M: L.tpo_gather_points_fwd(0, VP(1), VP(1), I64(N), I64(C), I64(P),
+                                                   I64(M), VP(1), VP(0))
+    assert g(1, -2, 4, 4) == 1
+    assert g(0, 3, 4, 4) == 0
 
 
 def test_workspace_checked():

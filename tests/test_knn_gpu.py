@@ -76,6 +76,35 @@ def test_knn_general_d(D):
     _run(p1, p2, l1, l2, 1, 7)
 
 
+@pytest.mark.parametrize("D,K", [(9, 5), (16, 32), (32, 7), (64, 3), (3, 33), (3, 64),
+                                 (12, 100), (2, 256)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float64, torch.float16])
+def test_knn_large_d_and_k(D, K, dtype):
+    """The general kernel: any D (the reference's V0/V1 range) and K up to 256."""
+    p1, p2, l1, l2 = _case(2, 70, 300, D, dtype, seed=D * 100 + K)
+    _run(p1, p2, l1, l2, 2, K)
+    _run(p1, p2, l1, l2, 1, K)
+
+
+def test_knn_large_k_ties():
+    g = torch.Generator().manual_seed(19)
+    p1 = torch.randint(0, 2, (2, 40, 10), generator=g).float()
+    p2 = torch.randint(0, 2, (2, 400, 10), generator=g).float()
+    _run(p1, p2, torch.tensor([40, 17]), torch.tensor([400, 90]), 2, 130)
+
+
+def test_knn_k_limit():
+    import ctypes
+
+    x = torch.zeros(1, 4, 3, device=DEV)
+    L = torch.full((1,), 4, device=DEV)
+    d = torch.empty(1, 4, 257, device=DEV)
+    i = torch.empty(1, 4, 257, dtype=torch.int64, device=DEV)
+    rc = C.lib().tpo_knn_fwd(0, 0, C.p(x), C.p(x), C.p(L), C.p(L), C.I64(1), C.I64(4), C.I64(4),
+                             C.I64(3), C.I64(2), C.I64(257), C.p(d), C.p(i), C.stream())
+    assert rc == 2  # TPO_ERR_UNSUPPORTED
+
+
 @pytest.mark.parametrize("dtype", [torch.float64, torch.float16])
 @pytest.mark.parametrize("norm", [1, 2])
 def test_knn_other_dtypes(dtype, norm):

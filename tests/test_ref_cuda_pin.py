@@ -98,3 +98,23 @@ def test_reference_gather_points_cuda():
     idx = torch.randint(0, 300, (2, 64), generator=g)
     ref = ops.gather_points_forward(pts.cuda(), idx.cuda()).cpu()
     assert torch.equal(C.gather_points_fwd(pts.cuda(), idx.cuda()).cpu(), ref)
+
+
+@pytest.mark.parametrize("D,K", [(16, 40), (40, 8), (3, 100)])
+def test_reference_knn_cuda_general(D, K):
+    """The reference's V1 / V0 kernels (D > 8 or K > 32) against the general path."""
+    ops = oracle.ref_knn()
+    if ops is None or not oracle._ref_loaded.get("knn_cuda_ref.so"):
+        pytest.skip("reference CUDA knn build not present in oracle/_ref")
+    g = torch.Generator().manual_seed(D * K)
+    p1 = torch.randn(2, 90, D, generator=g)
+    p2 = torch.randn(2, 400, D, generator=g)
+    L1 = torch.tensor([90, 61])
+    L2 = torch.tensor([400, 257])
+    ri, rd = ops.knn_forward(p1.cuda(), p2.cuda(), L1.cuda(), L2.cuda(), 2, K, -1)
+    rd, order = rd.sort(dim=2)
+    ri = ri.gather(2, order)
+    i, d = C.knn_fwd(p1.cuda(), p2.cuda(), L1.cuda(), L2.cuda(), 2, K, 0)
+    valid = torch.arange(90)[None, :, None] < L1[:, None, None]
+    assert torch.equal(i.cpu()[valid.expand_as(i.cpu())], ri.cpu()[valid.expand_as(i.cpu())])
+    assert np.array_equal(_bits(d.cpu()[valid.expand_as(d.cpu())]), _bits(rd.cpu()[valid.expand_as(d.cpu())]))

@@ -37,7 +37,7 @@ constexpr int KSTEP = 32;    // targets per step (one per lane)
 #define TPO_KTILE 2048
 #endif
 constexpr int KTILE = TPO_KTILE;  // targets per shared-memory tile
-constexpr int KDMAX = 8;
+constexpr int KDMAX = 8;     // the fast kernel's largest D
 
 template <typename T>
 struct KnnArith;
@@ -277,10 +277,151 @@ static int dispatch_knn_fwd(const void* p1, const void* p2, const int64_t* l1, c
                    : launch_knn_fwd<T, 0, 1, MODE>(a, b, l1, l2, N, P1, P2, (int)D, (int)K, o, idxs, st);
 }
 
+// ---- any D, K up to 32*KR: the general path (the reference's V0/V1 range) ----
+// One warp per query; the CTA's warps share nothing but L1 (targets are read
+// straight from global memory, lane c of a step taking target t0 + c, so every
+// D works without a shared-memory tile).  The running top-K list is spread over
+// the warp in KR rows: position p = r*32 + lane.  A candidate is accepted when
+// it beats the K-th entry and inserted by shifting every later position by one
+// (shuffle-up within a row, lane 31 of the row before feeding lane 0).  Same
+// acceptance/tie rule as the fast kernel: "K smallest by (dist, idx)".
+constexpr int KGW = 8;  // warps (queries) per CTA in the general kernel
+
+template <typename T, int NORM, int KR>
+__global__ void __launch_bounds__(KGW * 32)
+    knn_fwd_general_kernel(const T* __restrict__ p1, const T* __restrict__ p2,
+                           const int64_t* __restrict__ len1, const int64_t* __restrict__ len2,
+                           int64_t N, int64_t P1, int64_t P2, int D, int K, int64_t qblocks,
+                           T* __restrict__ dists, int64_t* __restrict__ idxs) {
+  using A = KnnArith<T>;
+  using V = typename A::V;
+  extern __shared__ __align__(16) unsigned char knn_gsmem[];
+  T* sq = reinterpret_cast<T*>(knn_gsmem) + (threadIdx.x >> 5) * D;  // this warp's query
+  const int lane = threadIdx.x & 31;
+  const int64_t n = blockIdx.x / qblocks;
+  const int64_t row = (blockIdx.x % qblocks) * KGW + (threadIdx.x >> 5);
+  if (row >= P1) return;  // whole warp: nothing to write
+  const int64_t L1 = len1 ? min64(max64(len1[n], 0), P1) : P1;
+  const int64_t L2 = len2 ? min64(max64(len2[n], 0), P2) : P2;
+  const bool qv = row < L1;
+  for (int d = lane; d < D; d += 32) sq[d] = p1[(n * P1 + row) * D + d];
+  __syncwarp();
+  V Ld[KR];
+  int Li[KR];
+#pragma unroll
+  for (int r = 0; r < KR; ++r) {
+    Ld[r] = (V)INFINITY;
+    Li[r] = -1;
+  }
+  V thr = (V)INFINITY;
+  const int kr_last = (K - 1) >> 5, kl_last = (K - 1) & 31;
+  if (qv) {
+    for (int64_t t0 = 0; t0 < L2; t0 += 32) {
+      const int64_t c = t0 + lane;
+      const bool cv = c < L2;
+      V dv = (V)INFINITY;
+      if (cv) {
+        const T* pc = p2 + (n * P2 + c) * D;
+        T t = NORM == 2 ? A::template sq_first<TPO_ROUND_EXACT>(sq[0], pc[0]) : A::abs_first(sq[0], pc[0]);
+        for (int d = 1; d < D; ++d)
+          t = NORM == 2 ? A::template sq_acc<TPO_ROUND_EXACT>(t, sq[d], pc[d]) : A::abs_acc(t, sq[d], pc[d]);
+        dv = A::val(t);
+      }
+      unsigned bal = __ballot_sync(0xffffffffu, cv && dv < thr);
+      while (bal) {
+        const int src = __ffs(bal) - 1;
+        bal &= bal - 1;
+        const V cd = __shfl_sync(0xffffffffu, dv, src);
+        if (!(cd < thr)) continue;
+        const int ci = (int)(t0 + src);
+        // shift every position holding a larger distance down by one, from the
+        // last row up (each row's lane 0 takes the previous row's lane 31 value
+        // before that row moves)
+#pragma unroll
+        for (int r = KR - 1; r >= 0; --r) {
+          V upd = __shfl_up_sync(0xffffffffu, Ld[r], 1);
+          int upi = __shfl_up_sync(0xffffffffu, Li[r], 1);
+          if (r > 0) {
+            const V pd = __shfl_sync(0xffffffffu, Ld[r - 1], 31);
+            const int pi = __shfl_sync(0xffffffffu, Li[r - 1], 31);
+            if (lane == 0) {
+              upd = pd;
+              upi = pi;
+            }
+          }
+          if (cd < Ld[r]) {
+            const bool take_prev = (lane > 0 || r > 0) && cd < upd;
+            Ld[r] = take_prev ? upd : cd;
+            Li[r] = take_prev ? upi : ci;
+          }
+        }
+        V kth = Ld[0];
+#pragma unroll
+        for (int r = 1; r < KR; ++r)
+          if (r == kr_last) kth = Ld[r];
+        thr = __shfl_sync(0xffffffffu, kth, kl_last);
+      }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < KR; ++r) {
+    const int k = r * 32 + lane;
+    if (k < K) {
+      const int64_t o = (n * P1 + row) * K + k;
+      const bool ok = qv && Li[r] >= 0;
+      dists[o] = ok ? A::from(Ld[r]) : T(0.0f);
+      idxs[o] = ok ? (int64_t)Li[r] : -1;
+    }
+  }
+}
+
+template <typename T, int NORM, int KR>
+static int launch_knn_general(const void* p1, const void* p2, const int64_t* l1, const int64_t* l2,
+                              int64_t N, int64_t P1, int64_t P2, int64_t D, int64_t K, void* dists,
+                              int64_t* idxs, cudaStream_t st) {
+  const int64_t qblocks = (P1 + KGW - 1) / KGW;
+  const int64_t ctas = N * qblocks;
+  if (ctas <= 0) return TPO_OK;
+  const size_t smem = (size_t)KGW * D * sizeof(T);
+  auto fn = knn_fwd_general_kernel<T, NORM, KR>;
+  if (smem > 48 * 1024)
+    if (int s = cuda_status(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)))
+      return s;
+  fn<<<(unsigned)ctas, KGW * 32, smem, st>>>((const T*)p1, (const T*)p2, l1, l2, N, P1, P2, (int)D,
+                                             (int)K, qblocks, (T*)dists, idxs);
+  return check_launch();
+}
+
+template <typename T, int NORM>
+static int dispatch_knn_general(const void* p1, const void* p2, const int64_t* l1, const int64_t* l2,
+                                int64_t N, int64_t P1, int64_t P2, int64_t D, int64_t K,
+                                void* dists, int64_t* idxs, cudaStream_t st) {
+  if (K <= 32) return launch_knn_general<T, NORM, 1>(p1, p2, l1, l2, N, P1, P2, D, K, dists, idxs, st);
+  if (K <= 64) return launch_knn_general<T, NORM, 2>(p1, p2, l1, l2, N, P1, P2, D, K, dists, idxs, st);
+  if (K <= 128) return launch_knn_general<T, NORM, 4>(p1, p2, l1, l2, N, P1, P2, D, K, dists, idxs, st);
+  return launch_knn_general<T, NORM, 8>(p1, p2, l1, l2, N, P1, P2, D, K, dists, idxs, st);
+}
+
+template <typename T>
+static int knn_general(const void* p1, const void* p2, const int64_t* l1, const int64_t* l2,
+                       int64_t N, int64_t P1, int64_t P2, int64_t D, int64_t norm, int64_t K,
+                       void* dists, int64_t* idxs, cudaStream_t st) {
+  return norm == 2 ? dispatch_knn_general<T, 2>(p1, p2, l1, l2, N, P1, P2, D, K, dists, idxs, st)
+                   : dispatch_knn_general<T, 1>(p1, p2, l1, l2, N, P1, P2, D, K, dists, idxs, st);
+}
+
 int knn_forward(int dtype, int flags, const void* p1, const void* p2, const int64_t* l1,
                 const int64_t* l2, int64_t N, int64_t P1, int64_t P2, int64_t D, int64_t norm,
                 int64_t K, void* dists, int64_t* idxs, cudaStream_t st) {
-  if (D > KDMAX || K > 32) return TPO_ERR_UNSUPPORTED;
+  if (K > kKnnMaxK) return TPO_ERR_UNSUPPORTED;
+  if (D > KDMAX || K > 32) {
+    switch (dtype) {
+      case TPO_F32: return knn_general<float>(p1, p2, l1, l2, N, P1, P2, D, norm, K, dists, idxs, st);
+      case TPO_F16: return knn_general<__half>(p1, p2, l1, l2, N, P1, P2, D, norm, K, dists, idxs, st);
+      case TPO_F64: return knn_general<double>(p1, p2, l1, l2, N, P1, P2, D, norm, K, dists, idxs, st);
+    }
+    return TPO_ERR_INVALID_ARGUMENT;
+  }
   // The reference knn kernels are compiled without contraction of
   // `dist += diff * diff` (measured on B200: bit-identical to the uncontracted
   // CPU path), so knn has a single rounding and ignores the flag.
@@ -346,6 +487,24 @@ __global__ void knn_bwd_kernel(const T* __restrict__ p1, const T* __restrict__ p
     const int64_t L1 = len1 ? len1[n] : P1;
     const int64_t L2 = len2 ? len2[n] : P2;
     const int kk = (int)min64(K, max64(L2, 0));
+    if (D > KDMAX) {  // general D: one coordinate at a time, same k order per coordinate
+      for (int d = 0; d < D; ++d) {
+        T acc = O::zero();
+        if (i < L1) {
+          for (int k = 0; k < kk; ++k) {
+            const int64_t j = idxs[t * K + k];
+            if (j < 0 || j >= P2) continue;
+            const T g = gd[t * K + k];
+            const T a = p1[t * D + d], b = p2[(n * P2 + j) * D + d];
+            const T v = norm == 1 ? O::l1(g, a, b) : O::l2(g, a, b);
+            acc = O::add(acc, v);
+            O::atomic_sub(g2 + (n * P2 + j) * D + d, v);
+          }
+        }
+        g1[t * D + d] = acc;
+      }
+      continue;
+    }
     T acc[KDMAX];
 #pragma unroll
     for (int d = 0; d < KDMAX; ++d) acc[d] = O::zero();
@@ -374,7 +533,6 @@ __global__ void knn_bwd_kernel(const T* __restrict__ p1, const T* __restrict__ p
 int knn_backward(int dtype, const void* p1, const void* p2, const int64_t* l1, const int64_t* l2,
                  const int64_t* idxs, int64_t N, int64_t P1, int64_t P2, int64_t D, int64_t K,
                  int64_t norm, const void* gd, void* g1, void* g2, cudaStream_t st) {
-  if (D > KDMAX) return TPO_ERR_UNSUPPORTED;
   const int64_t total = N * P1;
   if (total <= 0) return TPO_OK;
   const int threads = 256;
