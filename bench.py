@@ -57,7 +57,22 @@ CONFIGS = {
               desc="Chamfer fwd+bwd B=1 N=M=2^20 fp32 LiDAR-like (config 5)"),
     "5d": dict(kind="chamfer", B=1, N=1 << 20, M=1 << 20, dtype="float64", gen="lidar",
                desc="Chamfer fwd+bwd B=1 N=M=2^20 fp64 LiDAR-like (config 5, fp64)"),
+    # furthest point sampling: the reference fps_benchmark.py's "100K points" case
+    "fps": dict(kind="fps", B=1, N=100000, M=0, S=10000, dtype="float32", gen="normal",
+                desc="furthest_point_sampling B=1 P=100000 S=10000 fp32 N(0,1) (fps_benchmark.py)"),
+    "fpsb": dict(kind="fps", B=32, N=16384, M=0, S=1024, dtype="float32", gen="normal",
+                 desc="furthest_point_sampling B=32 P=16384 S=1024 fp32 N(0,1)"),
 }
+FPS_OPS_PER_UPDATE = 7  # 3 FADD + 1 FMUL + 2 FFMA + 1 FMNMX per point per step
+
+
+def metric_name(cfg):
+    return {"chamfer": "Chamfer fwd+bwd G point-pairs/s", "knn": "knn_points fwd+bwd G point-pairs/s",
+            "fps": "furthest_point_sampling G point-updates/s"}[cfg["kind"]]
+
+
+def unit_of(cfg):
+    return "Gupdate/s" if cfg["kind"] == "fps" else "Gpair/s"
 
 
 def dist_env():
@@ -149,10 +164,16 @@ def make_inputs(cfg, seed):
         return datagen.lidar(N, seed, dtype=dt), datagen.lidar(M, seed + 1, dtype=dt)
     if g == "knn4":
         return datagen.knn_config4(seed, dtype=dt, B=B, P=N)
+    if g == "normal":
+        return (torch.randn(B, N, 3, generator=torch.Generator().manual_seed(seed)).to(dt),)
     raise ValueError(g)
 
 
 def pairs_of(cfg, inputs):
+    """Work units per step: point pairs (chamfer, knn) or point updates (fps:
+    every point's running distance folds every new sample)."""
+    if cfg["kind"] == "fps":
+        return cfg["B"] * cfg["N"] * (cfg["S"] - 1)
     if cfg["kind"] == "knn":
         _, _, l1, l2 = inputs
         return int((l1.long() * l2.long()).sum())
@@ -169,6 +190,10 @@ def step_fn(cfg, sharded=False):
         def sstep(x1, x2):
             return sharded_chamfer_loss(x1.detach(), x2.detach())
         return sstep
+    if cfg["kind"] == "fps":
+        def fstep(x):
+            return (tpo.furthest_point_sampling(x, cfg["S"]),)
+        return fstep
     if cfg["kind"] == "chamfer":
         crit = tpo.ChamferDistance("mean")
 
@@ -188,9 +213,9 @@ def step_fn(cfg, sharded=False):
 
 
 def launches_per_step(cfg):
-    # chamfer: keys + finalize (fwd), scatter (bwd); knn: knn fwd, gather fwd,
-    # gather bwd, knn bwd
-    return 3 if cfg["kind"] == "chamfer" else 4
+    # chamfer: fill, keys, loss reduction (fwd), fill + scatter (bwd); knn: knn
+    # fwd, gather fwd, gather bwd, knn bwd; fps: one sampling kernel
+    return {"chamfer": 5, "knn": 4, "fps": 1}[cfg["kind"]]
 
 
 def run_ours(args, cfg):
@@ -208,7 +233,7 @@ def run_ours(args, cfg):
     host_inputs = make_inputs(cfg, seed=1000 if sharded else 1000 + 17 * rank)
     pairs = pairs_of(cfg, host_inputs)
     inputs = [t.to(dev) for t in host_inputs]
-    diff = [t.requires_grad_() if t.is_floating_point() else t for t in inputs]
+    diff = [t.requires_grad_() if t.is_floating_point() and cfg["kind"] != "fps" else t for t in inputs]
     step = step_fn(cfg, sharded)
     flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)  # 256 MiB > L2
 
@@ -294,9 +319,9 @@ def run_e2e(args, cfg, step, host_inputs, dev, flush, ws):
     def once():
         nonlocal outs_host
         xs = [t.to(dev, non_blocking=True) for t in pinned]
-        xs = [t.requires_grad_() if t.is_floating_point() else t for t in xs]
-        loss, g1, g2 = step(*xs)
-        outs = [loss.detach(), g1, g2]
+        if cfg["kind"] != "fps":
+            xs = [t.requires_grad_() if t.is_floating_point() else t for t in xs]
+        outs = [o.detach() for o in step(*xs)]
         if outs_host is None:
             outs_host = [torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in outs]
         for h, o in zip(outs_host, outs):
@@ -328,6 +353,8 @@ def kernel_roofline(cfg, inputs, dev, clocks, reps=20, rows=None):
     reports achieved pair throughput against the FP32-pipe roofline."""
     import torch_point_ops_b200 as tpo
 
+    if cfg["kind"] == "fps":
+        return fps_roofline(cfg, inputs, dev, clocks)
     if cfg["kind"] != "chamfer" or cfg["dtype"] != "float32":
         return None
     ops = tpo._lib.chamfer_ops
@@ -363,6 +390,36 @@ def kernel_roofline(cfg, inputs, dev, clocks, reps=20, rows=None):
         p2 = SMS * FP32_LANES * clocks["sm_mhz"] * 1e6 / INSTR_PER_PAIR / 1e9
         out["frac_at_measured_clock"] = round(achieved / p2, 4)
     return out
+
+
+def fps_roofline(cfg, inputs, dev, clocks, reps=5):
+    """FPS kernel alone: point updates per second against the FP32 pipe's bound
+    (7 pipe operations per update).  The kernel is bound by its step-to-step
+    latency chain (one group-wide exchange per sample), not by FLOPs or bytes,
+    so `frac` shows how far the sequential algorithm sits from the pipe."""
+    import torch_point_ops_b200 as tpo
+
+    x = inputs[0].detach()
+    S = cfg["S"]
+    for _ in range(2):
+        tpo.furthest_point_sampling(x, S)
+    tot = 0.0
+    for _ in range(reps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        tpo.furthest_point_sampling(x, S)
+        b.record()
+        b.synchronize()
+        tot += a.elapsed_time(b)
+    ms = tot / reps
+    ups = pairs_of(cfg, inputs)
+    achieved = ups / (ms * 1e-3) / 1e9
+    peak = SMS * FP32_LANES * MAX_SM_MHZ * 1e6 / FPS_OPS_PER_UPDATE / 1e9
+    return {"bound": "latency", "kernel": "fps_kernel", "achieved": round(achieved, 2),
+            "peak": round(peak, 1), "unit": "Gupdate/s", "frac": round(achieved / peak, 4),
+            "peak_basis": "nominal FP32 pipe: 148 SM x 128 lanes x 1965 MHz / 7 ops per update",
+            "kernel_ms": round(ms, 4), "us_per_sample": round(ms * 1e3 / (S - 1), 3),
+            "traffic": None}
 
 
 def profiled_traffic(cfg):
@@ -477,8 +534,38 @@ def cpu_knn_sample(cfg, host_inputs, max_rows=256, threads=None):
     return done, dt, kind, threads, f"{B} batches x first {max_rows} valid query rows, K={K} knn fwd+bwd, {threads} threads"
 
 
+def cpu_fps_sample(cfg, host_inputs, budget_s):
+    """The reference's CPU fps_forward (fps/csrc/fps.cpp:17-88, one thread per
+    call) on the full cloud with a reduced sample count sized to the budget."""
+    import concurrent.futures as cf
+
+    import oracle
+
+    ops = oracle.ref_fps()
+    x = host_inputs[0]
+    B, P = x.shape[0], x.shape[1]
+    threads = min(os.cpu_count() or 1, B)
+    run = (lambda xb, s: ops.fps_forward(xb, s)) if ops is not None else \
+        (lambda xb, s: oracle.fps(xb.numpy(), s))
+    kind = "reference" if ops is not None else "port"
+    t0 = time.perf_counter()
+    run(x[:1].contiguous(), 33)
+    probe = (time.perf_counter() - t0) / 32  # seconds per sample per cloud
+    S = int(max(2, min(cfg["S"], budget_s / 3 / max(probe, 1e-9) * threads / B)))
+    t0 = time.perf_counter()
+    with cf.ThreadPoolExecutor(threads) as ex:
+        list(ex.map(lambda b: run(x[b:b + 1].contiguous(), S), range(B)))
+    dt = time.perf_counter() - t0
+    return B * P * (S - 1), dt, kind, threads, (f"{B} cloud(s) x {P} points, {S} of {cfg['S']} samples, "
+                                                f"one thread per cloud ({threads} threads)")
+
+
 def cpu_measure(cfg, host_inputs, budget_s=15.0):
     """Bounded CPU sample (~budget_s); returns the cpu_baseline object."""
+    if cfg["kind"] == "fps":
+        done, dt, kind, cores, sample = cpu_fps_sample(cfg, host_inputs, budget_s)
+        return {"value": round(done / dt / 1e9, 4), "unit": "Gupdate/s", "cores": cores, "kind": kind,
+                "sample": sample, "seconds": round(dt, 3)}
     if cfg["kind"] == "knn":
         done, dt, kind, cores, sample = cpu_knn_sample(cfg, host_inputs)
     else:
@@ -511,7 +598,14 @@ def run_reference_cuda(args, cfg):
     host_inputs = make_inputs(cfg, seed=1000)
     pairs = pairs_of(cfg, host_inputs)
     x = [t.to(dev) for t in host_inputs]
-    if cfg["kind"] == "chamfer":
+    if cfg["kind"] == "fps":
+        ops = oracle.ref_fps()
+        if ops is None:
+            return {"impl": "reference_cuda", "unavailable": "oracle/_ref/fps_cuda_ref.so not built"}
+
+        def step():
+            return ops.fps_forward(x[0], cfg["S"])
+    elif cfg["kind"] == "chamfer":
         ops = oracle.ref_chamfer()
         if ops is None:
             return {"impl": "reference_cuda", "unavailable": "oracle/_ref/chamfer_cuda_ref.so not built"}
@@ -552,7 +646,7 @@ def run_reference_cuda(args, cfg):
         tot += a.elapsed_time(b)
     ms = tot / args.steps
     return {"impl": "reference_cuda", "metric": "reference CUDA kernels, same step (context)",
-            "value": round(pairs / (ms * 1e-3) / 1e9, 2), "unit": "Gpair/s",
+            "value": round(pairs / (ms * 1e-3) / 1e9, 2), "unit": unit_of(cfg),
             "ms_per_step": round(ms, 4), "config": {"workload": cfg["desc"]}}
 
 
@@ -573,15 +667,14 @@ def run_reference(args, cfg):
     v = statistics.median(vals)
     pairs = pairs_of(cfg, host_inputs)
     line = {
-        "impl": "reference", "metric": "Chamfer fwd+bwd G point-pairs/s" if cfg["kind"] == "chamfer"
-        else "knn_points fwd+bwd G point-pairs/s", "value": v, "unit": "Gpair/s",
+        "impl": "reference", "metric": metric_name(cfg), "value": v, "unit": unit_of(cfg),
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(pairs / (v * 1e9) * 1e3, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": cfg["dtype"].replace("float", "f"),
         "data": "synthetic (seeded, config distribution)",
         "config": {"workload": cfg["desc"]},
         "cpu_baseline": {k: last[k] for k in ("value", "unit", "cores", "kind", "sample")},
-        "e2e": {"value": v, "unit": "Gpair/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "e2e": {"value": v, "unit": unit_of(cfg), "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     line["cpu_baseline"]["value"] = v
     return line
@@ -620,9 +713,8 @@ def main():
         cpu = cpu_measure(cfg, make_inputs(cfg, seed=1000), budget_s=15.0)
         cpu = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
     line = {
-        "metric": "Chamfer fwd+bwd G point-pairs/s" if cfg["kind"] == "chamfer"
-        else "knn_points fwd+bwd G point-pairs/s",
-        "value": round(r["value"], 2), "unit": "Gpair/s", "n_gpus": ws, "steps": args.steps,
+        "metric": metric_name(cfg),
+        "value": round(r["value"], 2), "unit": unit_of(cfg), "n_gpus": ws, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(r["ms_per_step"], 4),
         "higher_is_better": True, "scaling": "strong" if r["sharded"] else "weak",
         "vs_baseline": None, "dtype": cfg["dtype"].replace("float", "f"),
@@ -633,7 +725,7 @@ def main():
                                    if r["sharded"] else f"dp{ws} (independent batch per GPU)"),
                    "cuda_graph": r["graph"]},
         "clocks": r["clocks"],
-        "e2e": {"value": round(r["e2e_value"], 2), "unit": "Gpair/s",
+        "e2e": {"value": round(r["e2e_value"], 2), "unit": unit_of(cfg),
                 "h2d_bytes_per_step": r["e2e"]["h2d"], "d2h_bytes_per_step": r["e2e"]["d2h"],
                 "ms_per_step": round(r["e2e"]["ms"], 4)},
         "gpu_launches": launches_per_step(cfg) * args.steps,

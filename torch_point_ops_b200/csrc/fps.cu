@@ -7,9 +7,10 @@
 // nine __syncthreads.  Here a cloud is spread over a GROUP of CTAs whose threads
 // hold their points and running distances in REGISTERS for the whole kernel;
 // a step is then: update PT points per thread (packed f32x2 / f16x2), one
-// redux.sync per warp, and an exchange of every warp's candidate -- through
-// shared memory and one CTA barrier (one CTA per cloud); by st.async pushes into
-// every CTA of a thread-block cluster, each CTA waiting on its own mbarrier (no
+// redux.sync per warp, and an exchange of the warps' candidates -- through
+// shared memory and one CTA barrier (one CTA per cloud); in a thread-block
+// cluster, the same CTA stage and then one st.async push of each CTA's winner
+// into every CTA of the cluster, each CTA waiting on its own mbarrier (no
 // cluster barrier); or through global memory and a grid barrier (cooperative
 // grid, for clouds larger than a cluster holds).  Work per step is O(P / (group threads)), latency a few
 // hundred cycles.
@@ -191,6 +192,11 @@ struct FpsF64 {
   static constexpr Key kMin = LLONG_MIN;
 };
 
+// Shared-memory candidate slots of one CTA (double-buffered).
+__host__ __device__ constexpr int fps_slot_count(int mode, int G, int NW) {
+  return mode == 2 ? 0 : mode == 1 ? 2 * (NW + G) : 2 * NW;
+}
+
 // Point index of virtual rank r (see the tie rule above); -1 for padding.
 __device__ __forceinline__ int fps_rank_to_index(int r, int P, int bs, int lbs, int Q) {
   const int c = r / Q, j = r - c * Q;
@@ -263,10 +269,10 @@ fps_kernel(const typename Tr::S* __restrict__ pts, int P, int S, int G, int bs, 
   using C = typename Tr::C;
   extern __shared__ __align__(16) unsigned char fps_smem[];
   const int NT = blockDim.x, NW = NT >> 5;
-  const int nsl = (MODE == kFpsCta ? 1 : G) * NW;  // candidate slots per step
   unsigned long long* bars = reinterpret_cast<unsigned long long*>(fps_smem);
   Slot* sslots = reinterpret_cast<Slot*>(fps_smem + 16);
-  Pt* spts = reinterpret_cast<Pt*>(fps_smem + 16 + 2 * (MODE == kFpsGrid ? 0 : nsl) * sizeof(Slot));
+  // CTA mode: slots [2][NW]; cluster mode: [2][NW] for the CTA stage, then [2][G]
+  Pt* spts = reinterpret_cast<Pt*>(fps_smem + 16 + fps_slot_count(MODE, G, NW) * sizeof(Slot));
   __shared__ int s_abort;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   int g = 0;
@@ -325,12 +331,12 @@ fps_kernel(const typename Tr::S* __restrict__ pts, int P, int S, int G, int bs, 
   else
     __syncthreads();
 
-  const int per = (nsl + 31) >> 5;
+  const int per = (G + 31) >> 5;  // grid mode: CTA slots per lane
   bool abort = false;
   for (int j = 1; j < S; ++j) {
     const int buf = j & 1;
     if (MODE == kFpsCluster && tid == 0)
-      mbar_expect_tx(&bars[buf], (unsigned)(nsl * sizeof(Slot)));
+      mbar_expect_tx(&bars[buf], (unsigned)(G * sizeof(Slot)));
     // 1. fold the newest sample into this thread's running distances
     const typename Tr::Sel s = Tr::sel(sx, sy, sz);
     Key tk = Tr::update(R[0], s);
@@ -343,6 +349,7 @@ fps_kernel(const typename Tr::S* __restrict__ pts, int P, int S, int G, int bs, 
     const Key wk = Tr::warp_max(tk);
     const int L = __ffs(__ballot_sync(0xffffffffu, tk == wk)) - 1;
     int mk = -1;  // the point index this lane proposed (lane L only)
+    C ex = C(0), ey = C(0), ez = C(0);
     const int my_slot = g * NW + warp;
     if (lane == L) {
       int p = 0;
@@ -353,23 +360,38 @@ fps_kernel(const typename Tr::S* __restrict__ pts, int P, int S, int G, int bs, 
       }
       const Pt e = spts[tid * PT + p];
       mk = e.k;
+      ex = e.x;
+      ey = e.y;
+      ez = e.z;
       Slot sl;
       sl.key = wk;
       sl.x = e.x;
       sl.y = e.y;
       sl.z = e.z;
-      if (MODE == kFpsGrid) {
-        slot_store_global(gslots + ((b * 2 + buf) * G + g) * NW + warp, sl);
-      } else if (MODE == kFpsCluster) {
-        const unsigned la = smem_addr(sslots + buf * nsl + my_slot), lb = smem_addr(&bars[buf]);
-        for (int c = 0; c < G; ++c) {
-          const unsigned ra = mapa_u32(la, c), rb = mapa_u32(lb, c);
+      sslots[buf * NW + warp] = sl;  // the CTA's warp slots [2][NW]
+    }
+    int cw = 0;  // cluster / grid mode: the CTA's winning warp
+    if (MODE != kFpsCta) {
+      // CTA stage: every warp reduces the CTA's warp slots (no second barrier)
+      __syncthreads();
+      Slot cv;
+      if (lane < NW) cv = sslots[buf * NW + lane]; else cv.key = Tr::kMin;
+      const Key ck = Tr::warp_max(cv.key);
+      cw = __ffs(__ballot_sync(0xffffffffu, cv.key == ck)) - 1;
+      Slot sl;
+      sl.key = ck;
+      sl.x = __shfl_sync(0xffffffffu, cv.x, cw);
+      sl.y = __shfl_sync(0xffffffffu, cv.y, cw);
+      sl.z = __shfl_sync(0xffffffffu, cv.z, cw);
+      if (MODE == kFpsGrid && tid == 0) slot_store_global(gslots + (b * 2 + buf) * G + g, sl);
+      if (MODE == kFpsCluster && warp == 0 && lane < G) {
+        // lane c pushes the CTA's winner into CTA c's slot [buf][g]
+        Slot* cl = sslots + 2 * NW;
+        const unsigned ra = mapa_u32(smem_addr(cl + buf * G + g), lane);
+        const unsigned rb = mapa_u32(smem_addr(&bars[buf]), lane);
 #pragma unroll
-          for (int i = 0; i < (int)(sizeof(Slot) / 16); ++i)
-            st_async16(ra + 16 * i, *(reinterpret_cast<const uint4*>(&sl) + i), rb);
-        }
-      } else {
-        sslots[buf * nsl + warp] = sl;
+        for (int i = 0; i < (int)(sizeof(Slot) / 16); ++i)
+          st_async16(ra + 16 * i, *(reinterpret_cast<const uint4*>(&sl) + i), rb);
       }
     }
     // 3. wait until every candidate of the group is visible
@@ -401,29 +423,41 @@ fps_kernel(const typename Tr::S* __restrict__ pts, int P, int S, int G, int bs, 
             s_abort = 1;
             break;
           }
-          __nanosleep(64);
         }
         __threadfence();
       }
       __syncthreads();
       if (s_abort) return;
     }
-    // 4. group winner over all slots (each lane a contiguous run: lowest slot wins ties)
+    // 4. group winner over the slots (warps in CTA mode, CTAs otherwise); lanes
+    // take contiguous runs, so the lowest slot wins ties
     Key bk = Tr::kMin;
     int bslot = 0;
     C bx = C(0), by = C(0), bz = C(0);
-    for (int i = 0; i < per; ++i) {
-      const int si = lane * per + i;
-      if (si < nsl) {
-        const Slot v = MODE == kFpsGrid ? slot_load_global(gslots + ((b * 2 + buf) * G) * NW + si)
-                                        : sslots[buf * nsl + si];
-        if (v.key > bk) {
-          bk = v.key;
-          bslot = si;
-          bx = v.x;
-          by = v.y;
-          bz = v.z;
+    if (MODE == kFpsGrid) {
+      for (int i = 0; i < per; ++i) {
+        const int si = lane * per + i;
+        if (si < G) {
+          const Slot v = slot_load_global(gslots + (b * 2 + buf) * G + si);
+          if (v.key > bk) {
+            bk = v.key;
+            bslot = si;
+            bx = v.x;
+            by = v.y;
+            bz = v.z;
+          }
         }
+      }
+    } else {
+      const int n2 = MODE == kFpsCluster ? G : NW;
+      const Slot* base = MODE == kFpsCluster ? sslots + 2 * NW + buf * G : sslots + buf * NW;
+      if (lane < n2) {
+        const Slot v = base[lane];
+        bk = v.key;
+        bslot = lane;
+        bx = v.x;
+        by = v.y;
+        bz = v.z;
       }
     }
     const Key gk = Tr::warp_max(bk);
@@ -437,7 +471,7 @@ fps_kernel(const typename Tr::S* __restrict__ pts, int P, int S, int G, int bs, 
       sy = p0y;
       sz = p0z;
       if (g == 0 && tid == 0) bo[j] = 0;
-    } else if (lane == L && wslot == (MODE == kFpsCta ? warp : my_slot)) {
+    } else if (lane == L && (MODE == kFpsCta ? wslot == warp : (wslot == g && cw == warp))) {
       bo[j] = mk;
     }
   }
@@ -471,8 +505,7 @@ static int64_t fps_virtual_points(int64_t P) {
 
 template <class Tr>
 static size_t fps_smem_bytes(int mode, int G, int NT, int PT) {
-  const int nsl = (mode == kFpsCta ? 1 : G) * (NT / 32);
-  return 16 + (mode == kFpsGrid ? 0 : 2 * nsl * sizeof(typename Tr::Slot)) +
+  return 16 + fps_slot_count(mode, G, NT / 32) * sizeof(typename Tr::Slot) +
          (size_t)NT * PT * sizeof(typename Tr::Pt);
 }
 
@@ -529,17 +562,17 @@ static int fps_cluster_capacity(int G, int NT, int PT, int* out) {
   return cuda_status(cudaOccupancyMaxActiveClusters(out, fn, &cfg));
 }
 
-// Estimated cycles of one sampling step for a group shape (see the kernel's
-// step: update, warp reduce, barrier, slot reads).  Constants from B200
-// measurements of this kernel.
+// Estimated cycles of one sampling step for a group shape: the running-distance
+// update (about 9 cycles per point per resident warp of a scheduler; fp64
+// twice that) plus the exchange's fixed latency (warp reduce, candidate pick,
+// barrier or push + wait, final reduce), measured on B200 for each mode.
 static double fps_step_cycles(int dtype, int mode, int G, int NT, int PT) {
-  const double per_pt = dtype == TPO_F64 ? 8.0 : 5.0;
+  const double per_pt = dtype == TPO_F64 ? 18.0 : 9.0;
   const int NW = NT / 32;
-  const double issue = per_pt * PT * ((NW + 3) / 4);  // 4 schedulers per SM
-  double c = issue + 2.0 * PT + 120.0;                 // + lane scan, warp reduce, slot write
-  if (mode == kFpsCta) c += NW > 1 ? 60.0 : 10.0;
-  if (mode == kFpsCluster) c += 300.0 + 2.0 * G + 4.0 * ((G * NW + 31) / 32);
-  if (mode == kFpsGrid) c += 1800.0 + 30.0 * ((G * NW + 31) / 32);
+  double c = per_pt * PT * ((NW + 3) / 4);  // 4 schedulers per SM
+  if (mode == kFpsCta) c += NW > 1 ? 650.0 : 550.0;
+  if (mode == kFpsCluster) c += 950.0 + 5.0 * G;
+  if (mode == kFpsGrid) c += 7000.0 + 30.0 * ((G + 31) / 32);
   return c;
 }
 
@@ -593,9 +626,9 @@ static int fps_plan(int dtype, int64_t B, int64_t P, FpsPlan* plan) {
 static size_t fps_ws_bytes_for(int dtype, int64_t B, const FpsPlan& p) {
   if (p.mode != kFpsGrid) return 0;
   const size_t slot = dtype == TPO_F64 ? sizeof(FpsSlotD) : sizeof(FpsSlotF);
-  // counters, then slots [B][2][G*NW]
+  // counters, then slots [B][2][G]
   const size_t cnt = ((size_t)B * 4 + 255) & ~(size_t)255;
-  return cnt + (size_t)B * 2 * p.G * (p.NT / 32) * slot;
+  return cnt + (size_t)B * 2 * p.G * slot;
 }
 
 template <class Tr>
