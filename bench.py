@@ -306,7 +306,8 @@ def run_ours(args, cfg):
         from torch_point_ops_b200.sharded import row_range
         rows = row_range(cfg["N"], ws, rank)
     roof = kernel_roofline(cfg, inputs, dev, clk.summary(), rows=rows)
-    return dict(value=value, ms_per_step=ms_per_step, pairs=pairs, graph=graph is not None,
+    roof_bwd = None if sharded else bwd_roofline(cfg, inputs, dev)
+    return dict(roofline_bwd=roof_bwd, value=value, ms_per_step=ms_per_step, pairs=pairs, graph=graph is not None,
                 sharded=sharded,
                 clocks=clk.summary(), e2e=e2e, e2e_value=e2e_value, roofline=roof)
 
@@ -390,6 +391,48 @@ def kernel_roofline(cfg, inputs, dev, clocks, reps=20, rows=None):
         p2 = SMS * FP32_LANES * clocks["sm_mhz"] * 1e6 / INSTR_PER_PAIR / 1e9
         out["frac_at_measured_clock"] = round(achieved / p2, 4)
     return out
+
+
+def measured_hbm_gbs():
+    """HBM copy bandwidth of this pool's B200s (MEASURED_PEAKS.json), else the
+    recipe's fallback."""
+    try:
+        return float(json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def bwd_roofline(cfg, inputs, dev, reps=20):
+    """The chamfer backward alone (the loss op's backward: zero-fill + gradient
+    scatter) against HBM: algorithmic bytes B*(N+M)*(7s+4) per step -- own
+    coordinates 3s, neighbour index 4, upstream grad s, neighbour coordinates 3s
+    -- over its device time."""
+    import torch_point_ops_b200 as tpo
+
+    if cfg["kind"] != "chamfer":
+        return None
+    x1, x2 = [t.detach().clone().requires_grad_() for t in inputs[:2]]
+    loss = tpo.ChamferDistance("mean")(x1, x2)
+    for _ in range(3):
+        torch.autograd.grad(loss, [x1, x2], retain_graph=True)
+    flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)
+    tot = 0.0
+    for i in range(reps):
+        flush_l2(flush, i)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        torch.autograd.grad(loss, [x1, x2], retain_graph=True)
+        b.record()
+        b.synchronize()
+        tot += a.elapsed_time(b)
+    ms = tot / reps
+    s = x1.element_size()
+    nbytes = cfg["B"] * (cfg["N"] + cfg["M"]) * (7 * s + 4)
+    peak, basis = measured_hbm_gbs()
+    ach = nbytes / (ms * 1e-3) / 1e9
+    return {"bound": "hbm", "kernel": "chamfer_bwd_from_keys_kernel (+ zero-fill)", "achieved": round(ach, 1),
+            "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4), "peak_basis": basis,
+            "algorithmic_bytes": nbytes, "ms": round(ms, 4)}
 
 
 def fps_roofline(cfg, inputs, dev, clocks, reps=5):
@@ -610,13 +653,24 @@ def run_reference_cuda(args, cfg):
         if ops is None:
             return {"impl": "reference_cuda", "unavailable": "oracle/_ref/chamfer_cuda_ref.so not built"}
         B, N, M = cfg["B"], cfg["N"], cfg["M"]
+        if N * M > (1 << 36):
+            # config 5: the reference forward on a 32768-row subsample of cloud 1
+            # against all of cloud 2 (one launch does both directions of its
+            # inputs, i.e. 32768 x M unordered pairs); forward only, rate
+            # extrapolates linearly
+            sub = 1 << 15
+            a1 = x[0][:, :sub].contiguous()
+            pairs = B * sub * M
 
-        def step():
-            d1, d2, i1, i2 = ops.chamfer_forward(x[0], x[1])
-            loss = d1.mean() + d2.mean()
-            g1 = torch.full_like(d1, 1.0 / (B * N))
-            g2 = torch.full_like(d2, 1.0 / (B * M))
-            return loss, ops.chamfer_backward(x[0], x[1], i1, i2, g1, g2)
+            def step():
+                return ops.chamfer_forward(a1, x[1])
+        else:
+            def step():
+                d1, d2, i1, i2 = ops.chamfer_forward(x[0], x[1])
+                loss = d1.mean() + d2.mean()
+                g1 = torch.full_like(d1, 1.0 / (B * N))
+                g2 = torch.full_like(d2, 1.0 / (B * M))
+                return loss, ops.chamfer_backward(x[0], x[1], i1, i2, g1, g2)
     else:
         ops = oracle.ref_knn()
         if ops is None or not oracle._ref_loaded.get("knn_cuda_ref.so"):
@@ -730,6 +784,7 @@ def main():
                 "ms_per_step": round(r["e2e"]["ms"], 4)},
         "gpu_launches": launches_per_step(cfg) * args.steps,
         "roofline": r["roofline"],
+        "roofline_bwd": r["roofline_bwd"],
         "cpu_baseline": cpu,
     }
     print(json.dumps(line), flush=True)
