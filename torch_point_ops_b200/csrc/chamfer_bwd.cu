@@ -142,6 +142,7 @@ __global__ void fill_prefetch_kernel(unsigned char* d0, size_t n0, unsigned char
   const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   const size_t nth = (size_t)gridDim.x * blockDim.x;
   const uint4 v = make_uint4(v32, v32, v32, v32);
+  pdl_trigger();  // the (PDL-launched) consumer may be scheduled; it waits for this grid
   for (int r = 0; r < 2; ++r) {
     unsigned char* d = r ? d1 : d0;
     const size_t n = r ? n1 : n0;

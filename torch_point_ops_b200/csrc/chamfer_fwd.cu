@@ -102,6 +102,7 @@ __global__ void __launch_bounds__(CF_MAXW * 32, TPO_CF_MINB)
   __shared__ __align__(16) float2 s_col[CF_TILE_STEPS][3][CF_C];
   __shared__ __align__(16) uint2 s_wb[CF_MAXW][CF_TILE];  // {ballot, distance bits}
 
+  pdl_wait();  // launched with programmatic serialisation: inputs/keys ready after this
   const int W = blockDim.x >> 5;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -268,6 +269,7 @@ __global__ void __launch_bounds__(CF_MAXW * 32, TPO_CF_MINB)
                     ((u64)__float_as_uint(best[r]) << 32) | (unsigned)bchunk[r]);
     }
   }
+  pdl_trigger();  // the next kernel may be scheduled (it waits for this grid)
 }
 
 // ----------------------------- fp16 fast path -----------------------------
@@ -292,6 +294,7 @@ __global__ void __launch_bounds__(CF_MAXW * 32, TPO_CF_MINB)
   __shared__ __align__(16) uint2 s_wb[CF_MAXW][CF_TILE];  // {ballot, half distance bits}
   __shared__ __align__(16) __half s_rows[CF_MAXW * CF_ROWS_PER_WARP * 3];
 
+  pdl_wait();  // launched with programmatic serialisation: inputs/keys ready after this
   const int W = blockDim.x >> 5;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -456,6 +459,7 @@ __global__ void __launch_bounds__(CF_MAXW * 32, TPO_CF_MINB)
       }
     }
   }
+  pdl_trigger();  // the next kernel may be scheduled (it waits for this grid)
 }
 
 // ------------------------- fp16 / fp64 generic path -------------------------
@@ -549,6 +553,7 @@ __global__ void __launch_bounds__(CG_MAXW * 32)
   __shared__ __align__(16) T s_col[CG_TILE_STEPS][3][CG_C];
   __shared__ __align__(16) K s_key[CG_MAXW][CG_TILE];
 
+  pdl_wait();  // launched with programmatic serialisation: inputs/keys ready after this
   const int W = blockDim.x >> 5;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -640,6 +645,7 @@ __global__ void __launch_bounds__(CG_MAXW * 32)
       if (row < row_end) KO::flush(keys1 + b * N + row, KO::make(best[r], (unsigned)bchunk[r]));
     }
   }
+  pdl_trigger();  // the next kernel may be scheduled (it waits for this grid)
 }
 
 // ------------------------------- finalize -------------------------------
@@ -746,6 +752,7 @@ __global__ void chamfer_finalize_kernel(const T* __restrict__ xyz1, const T* __r
                                         T* __restrict__ dist2, int32_t* __restrict__ idx2,
                                         bool do_cols, FinLoss<T> fl) {
   using F = FinTraits<T>;
+  pdl_wait();
   const int64_t nrows = row_end - row_begin;
   const int64_t n1 = B * nrows;
   const int64_t total = n1 + (do_cols ? B * M : 0);
@@ -882,6 +889,7 @@ __global__ void chamfer_bwd_from_keys_kernel(const T* __restrict__ xyz1, const T
                                              const T* __restrict__ grad_loss, int reduction,
                                              T* __restrict__ gx1, T* __restrict__ gx2) {
   using O = FkOps<T>;
+  pdl_wait();
   const T g = *grad_loss;
   const T g1 = O::scale(g, B * N, reduction);
   const T g2 = O::scale(g, B * M, reduction);
@@ -976,9 +984,8 @@ int launch_keys_f32(const float* x1, const float* x2, int64_t B, int64_t N, int6
   if (!slots) slots = slots_for(kern, CF_MAXW * 32);
   const Plan p = make_plan(B, rb1 - rb0, M, CF_ROWS_PER_WARP, CF_MAXW, slots);
   if (p.ctas <= 0) return TPO_OK;
-  kern<<<(unsigned)p.ctas, p.warps * 32, 0, st>>>(x1, x2, N, M, rb0, rb1, p.rb_count, p.cs_count,
-                                                   p.seg, (u64*)k1, (u64*)k2);
-  return check_launch();
+  return launch_pdl(kern, dim3((unsigned)p.ctas), dim3(p.warps * 32), 0, st, x1, x2, N, M, rb0, rb1,
+                    p.rb_count, p.cs_count, p.seg, (u64*)k1, (u64*)k2);
 }
 
 int launch_keys_f16(const __half* x1, const __half* x2, int64_t B, int64_t N, int64_t M,
@@ -991,9 +998,8 @@ int launch_keys_f16(const __half* x1, const __half* x2, int64_t B, int64_t N, in
   if (!slots) slots = slots_for(kern, CF_MAXW * 32);
   const Plan p = make_plan(B, rb1 - rb0, M, CF_ROWS_PER_WARP, CF_MAXW, slots);
   if (p.ctas <= 0) return TPO_OK;
-  kern<<<(unsigned)p.ctas, p.warps * 32, 0, st>>>(x1, x2, N, M, rb0, rb1, p.rb_count, p.cs_count,
-                                                   p.seg, (u64*)k1, (u64*)k2);
-  return check_launch();
+  return launch_pdl(kern, dim3((unsigned)p.ctas), dim3(p.warps * 32), 0, st, x1, x2, N, M, rb0, rb1,
+                    p.rb_count, p.cs_count, p.seg, (u64*)k1, (u64*)k2);
 }
 
 template <typename T, int MODE>
@@ -1008,9 +1014,8 @@ int launch_keys_generic(const T* x1, const T* x2, int64_t B, int64_t N, int64_t 
   if (!slots) slots = slots_for(kern, CG_MAXW * 32);
   const Plan p = make_plan(B, rb1 - rb0, M, CG_ROWS_PER_WARP, CG_MAXW, slots);
   if (p.ctas <= 0) return TPO_OK;
-  kern<<<(unsigned)p.ctas, p.warps * 32, 0, st>>>(x1, x2, N, M, rb0, rb1, p.rb_count, p.cs_count,
-                                                   p.seg, (K*)k1, (K*)k2);
-  return check_launch();
+  return launch_pdl(kern, dim3((unsigned)p.ctas), dim3(p.warps * 32), 0, st, x1, x2, N, M, rb0, rb1,
+                    p.rb_count, p.cs_count, p.seg, (K*)k1, (K*)k2);
 }
 
 template <typename T, int MODE, int ROWCH, int COLCH>
@@ -1028,10 +1033,9 @@ int launch_finalize(const T* x1, const T* x2, int64_t B, int64_t N, int64_t M, i
   fl.reduction = reduction;
   fl.partials = (double*)loss_ws;
   fl.counter = loss_ws ? (unsigned*)((char*)loss_ws + kFinPartialBytes) : nullptr;
-  chamfer_finalize_kernel<T, MODE, ROWCH, COLCH><<<(unsigned)blocks, threads, 0, st>>>(
-      x1, x2, B, N, M, rb0, rb1, (const typename FinTraits<T>::K*)k1,
-      (const typename FinTraits<T>::K*)k2, d1, i1, d2, i2, do_cols, fl);
-  return check_launch();
+  return launch_pdl(chamfer_finalize_kernel<T, MODE, ROWCH, COLCH>, dim3((unsigned)blocks), dim3(threads), 0,
+                    st, x1, x2, B, N, M, rb0, rb1, (const typename FinTraits<T>::K*)k1,
+                    (const typename FinTraits<T>::K*)k2, d1, i1, d2, i2, do_cols, fl);
 }
 
 }  // namespace
@@ -1083,6 +1087,7 @@ __global__ void keys_loss_reduce_kernel(const u64* __restrict__ k1, int64_t n1,
                                         double* __restrict__ part, unsigned* ctr, void* loss,
                                         int half_out, int reduction) {
   __shared__ double sa[32], sc[32];
+  pdl_wait();
   double a = 0.0, c = 0.0;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n1;
        i += (int64_t)gridDim.x * blockDim.x)
@@ -1130,10 +1135,9 @@ int chamfer_loss_keys(int dtype, int flags, const void* x1, const void* x2, int6
   const int64_t want = (B * (N + M) + threads * 8 - 1) / (threads * 8);
   const unsigned blocks = (unsigned)std::max<int64_t>(1, std::min<int64_t>(want, 296));
   unsigned* ctr = (unsigned*)lossws + B;  // the 0xff-filled counter word after the batch counters
-  keys_loss_reduce_kernel<<<blocks, threads, 0, st>>>((const u64*)k1, B * N, (const u64*)k2, B * M,
-                                                      (double*)partials, ctr, loss,
-                                                      dtype == TPO_F16, reduction);
-  return check_launch();
+  return launch_pdl(keys_loss_reduce_kernel, dim3(blocks), dim3(threads), 0, st, (const u64*)k1, B * N,
+                    (const u64*)k2, B * M, (double*)partials, ctr, loss, (int)(dtype == TPO_F16),
+                    reduction);
 }
 
 int chamfer_bwd_from_keys(int dtype, int flags, const void* x1, const void* x2, int64_t B,
@@ -1148,18 +1152,16 @@ int chamfer_bwd_from_keys(int dtype, int flags, const void* x1, const void* x2, 
   const u64* K1 = (const u64*)k1;
   const u64* K2 = (const u64*)k2;
   if (dtype == TPO_F16)
-    chamfer_bwd_from_keys_kernel<__half, TPO_ROUND_EXACT><<<blocks, threads, 0, st>>>(
-        (const __half*)x1, (const __half*)x2, B, N, M, K1, K2, (const __half*)grad_loss,
-        reduction, (__half*)gx1, (__half*)gx2);
-  else if (exact)
-    chamfer_bwd_from_keys_kernel<float, TPO_ROUND_EXACT><<<blocks, threads, 0, st>>>(
-        (const float*)x1, (const float*)x2, B, N, M, K1, K2, (const float*)grad_loss, reduction,
-        (float*)gx1, (float*)gx2);
-  else
-    chamfer_bwd_from_keys_kernel<float, TPO_ROUND_FMA><<<blocks, threads, 0, st>>>(
-        (const float*)x1, (const float*)x2, B, N, M, K1, K2, (const float*)grad_loss, reduction,
-        (float*)gx1, (float*)gx2);
-  return check_launch();
+    return launch_pdl(chamfer_bwd_from_keys_kernel<__half, TPO_ROUND_EXACT>, dim3(blocks), dim3(threads), 0, st,
+                      (const __half*)x1, (const __half*)x2, B, N, M, K1, K2, (const __half*)grad_loss,
+                      reduction, (__half*)gx1, (__half*)gx2);
+  if (exact)
+    return launch_pdl(chamfer_bwd_from_keys_kernel<float, TPO_ROUND_EXACT>, dim3(blocks), dim3(threads), 0, st,
+                      (const float*)x1, (const float*)x2, B, N, M, K1, K2, (const float*)grad_loss,
+                      reduction, (float*)gx1, (float*)gx2);
+  return launch_pdl(chamfer_bwd_from_keys_kernel<float, TPO_ROUND_FMA>, dim3(blocks), dim3(threads), 0, st,
+                    (const float*)x1, (const float*)x2, B, N, M, K1, K2, (const float*)grad_loss,
+                    reduction, (float*)gx1, (float*)gx2);
 }
 
 int device_error_flags(unsigned* out, bool clear) {

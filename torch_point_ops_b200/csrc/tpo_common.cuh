@@ -241,6 +241,14 @@ __device__ __forceinline__ bool mbar_wait(unsigned long long* bar, unsigned pari
   return false;
 }
 
+// Programmatic dependent launch.  A kernel launched with launch_pdl may start
+// while the previous kernel in the stream is still running; it must call
+// pdl_wait() before touching global memory (that returns once the previous
+// grid has completed and its writes are visible).  pdl_trigger() lets the next
+// kernel's CTAs be scheduled early; both are no-ops without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ unsigned lane_id() {
   unsigned r;
   asm("mov.u32 %0, %%laneid;" : "=r"(r));

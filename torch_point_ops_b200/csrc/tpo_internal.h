@@ -77,6 +77,23 @@ int gather_points_forward(int dtype, const void* pts, const int64_t* idx, int64_
 int gather_points_backward(int dtype, const void* gout, const int64_t* idx, int64_t N, int64_t C,
                            int64_t P, int64_t M, void* gpts, cudaStream_t st);
 
+// Launches `kern` with programmatic stream serialisation allowed (see pdl_wait).
+template <typename... KArgs, typename... Args>
+inline int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                      Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...));
+}
+
 inline int dtype_size(int dtype) {
   return dtype == TPO_F32 ? 4 : dtype == TPO_F16 ? 2 : dtype == TPO_F64 ? 8 : 0;
 }
