@@ -161,6 +161,18 @@ TPO_API int tpo_chamfer_loss_bwd(int dtype, int flags, const void* xyz1, const v
                                  const void* workspace, const void* grad_loss, void* grad_xyz1,
                                  void* grad_xyz2, void* stream);
 
+/* Backward of the fused loss without a gradient fill: tpo_chamfer_loss_fwd also
+ * zero-fills a gradient region inside the workspace (in the launch that resets
+ * the keys), and this call scatters the gradients there -- grad_xyz1 (B,N,3) at
+ * byte offset tpo_chamfer_loss_grad_offset(...,1) of the workspace, grad_xyz2
+ * (B,M,3) at offset tpo_chamfer_loss_grad_offset(...,2), both 256-byte
+ * aligned.  Valid once per forward (a second backward of the same forward must
+ * use tpo_chamfer_loss_bwd, which fills caller buffers). */
+TPO_API size_t tpo_chamfer_loss_grad_offset(int dtype, int64_t B, int64_t N, int64_t M, int which);
+TPO_API int tpo_chamfer_loss_bwd_workspace(int dtype, int flags, const void* xyz1, const void* xyz2,
+                                           int64_t B, int64_t N, int64_t M, int reduction,
+                                           void* workspace, const void* grad_loss, void* stream);
+
 /* ------------------------------------------------------------------------- */
 /* K nearest neighbours forward.  Replaces knn_cuda_forward
  * (torch_point_ops/knn/csrc/cuda/knn.cu:295-398) behind

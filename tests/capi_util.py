@@ -163,3 +163,21 @@ def gather_points_bwd(gout, idx, P):
     check(lib().tpo_gather_points_bwd(DT[gout.dtype], p(gout), p(idx), I64(B), I64(Cc), I64(P),
                                       I64(S), p(gp), stream()))
     return gp
+
+
+def chamfer_loss_bwd_in_state(x1, x2, state, grad_loss, reduction=0, flags=0):
+    """tpo_chamfer_loss_bwd_workspace: gradients scattered into the forward's
+    zeroed gradient region; returned as views of the workspace."""
+    B, N, _ = x1.shape
+    M = x2.shape[1]
+    dt = DT[x1.dtype]
+    check(lib().tpo_chamfer_loss_bwd_workspace(dt, flags, p(x1), p(x2), I64(B), I64(N), I64(M),
+                                               ctypes.c_int(reduction), p(state), p(grad_loss),
+                                               stream()))
+    lib().tpo_chamfer_loss_grad_offset.restype = ctypes.c_size_t
+    o1 = lib().tpo_chamfer_loss_grad_offset(dt, I64(B), I64(N), I64(M), 1)
+    o2 = lib().tpo_chamfer_loss_grad_offset(dt, I64(B), I64(N), I64(M), 2)
+    es = x1.element_size()
+    g1 = state[o1:o1 + es * 3 * B * N].view(x1.dtype).view(B, N, 3)
+    g2 = state[o2:o2 + es * 3 * B * M].view(x1.dtype).view(B, M, 3)
+    return g1, g2

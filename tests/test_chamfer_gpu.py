@@ -219,6 +219,42 @@ def test_fused_loss_capi(dtype, reduction, shape):
     assert np.all(e2 <= 2 * tolerance(dtype, s2, n2))
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float64, torch.float16])
+@pytest.mark.parametrize("shape", [(3, 1111, 777), (1, 1, 1), (2, 0, 5)])
+def test_fused_loss_backward_in_workspace(dtype, shape):
+    """The fill-free backward (gradients in the forward's zeroed workspace region)
+    equals the backward into caller buffers."""
+    B, N, M = shape
+    x1 = datagen.sphere_noise(B, N, seed=18, dtype=dtype).to(DEV)
+    x2 = datagen.sphere_noise(B, M, seed=19, dtype=dtype).to(DEV)
+    loss, state = C.chamfer_loss_fwd(x1, x2, 0)
+    gl = torch.tensor([1.25], dtype=dtype, device=DEV)
+    r1, r2 = C.chamfer_loss_bwd(x1, x2, state, gl, 0)
+    w1, w2 = C.chamfer_loss_bwd_in_state(x1, x2, state, gl, 0)
+    tol = {torch.float32: 1e-6, torch.float64: 1e-12, torch.float16: 2e-3}[dtype]
+    torch.testing.assert_close(w1, r1, rtol=tol, atol=tol)
+    torch.testing.assert_close(w2, r2, rtol=tol, atol=tol)
+
+
+def test_chamfer_distance_module_double_backward_call():
+    """A second backward of the same forward (retain_graph) must not accumulate
+    onto the first one's in-workspace gradients."""
+    import torch_point_ops_b200 as tpo
+
+    x1 = datagen.sphere_noise(2, 500, seed=21).to(DEV).requires_grad_()
+    x2 = datagen.sphere_noise(2, 400, seed=22).to(DEV).requires_grad_()
+    loss = tpo.ChamferDistance("mean")(x1, x2)
+    a1, a2 = torch.autograd.grad(loss, [x1, x2], retain_graph=True)
+    a1, a2 = a1.clone(), a2.clone()
+    b1, b2 = torch.autograd.grad(loss, [x1, x2])
+    torch.testing.assert_close(a1, b1, rtol=1e-6, atol=1e-9)
+    torch.testing.assert_close(a2, b2, rtol=1e-6, atol=1e-9)
+    # and a plain .backward() accumulates into .grad as usual
+    loss2 = tpo.ChamferDistance("mean")(x1, x2)
+    loss2.backward()
+    torch.testing.assert_close(x1.grad, a1, rtol=1e-6, atol=1e-9)
+
+
 def test_fused_loss_two_calls_deterministic():
     x1 = datagen.gmm(4, 3000, seed=3).to(DEV)
     x2 = datagen.gmm(4, 2000, seed=4).to(DEV)

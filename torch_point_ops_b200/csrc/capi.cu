@@ -181,7 +181,7 @@ int tpo_chamfer_bwd_partial(int dtype, const void* xyz1, const void* xyz2, int64
 // backward re-derives the neighbours from the keys; other cases finalize into
 // idx1/idx2 and reduce there.
 struct LossLayout {
-  size_t keys, kl, fin, idx1, idx2, total;
+  size_t keys, kl, fin, idx1, idx2, g1, g2, total;
 };
 static LossLayout loss_layout(int dtype, int64_t B, int64_t N, int64_t M) {
   LossLayout L;
@@ -190,7 +190,11 @@ static LossLayout loss_layout(int dtype, int64_t B, int64_t N, int64_t M) {
   L.fin = L.kl + keys_loss_bytes(B);
   L.idx1 = L.fin + align256(kFinLossWorkspace);
   L.idx2 = L.idx1 + align256(4 * (size_t)B * (size_t)N);
-  L.total = L.idx2 + align256(4 * (size_t)B * (size_t)M);
+  // gradient region, zero-filled by the forward (tpo_chamfer_loss_bwd_workspace)
+  const size_t es = (size_t)dtype_size(dtype);
+  L.g1 = L.idx2 + align256(4 * (size_t)B * (size_t)M);
+  L.g2 = L.g1 + align256(es * 3 * (size_t)B * (size_t)N);
+  L.total = L.g2 + align256(es * 3 * (size_t)B * (size_t)M);
   return L;
 }
 static bool loss_uses_keys_kernel(int dtype, int64_t B, int64_t N, int64_t M) {
@@ -221,20 +225,39 @@ int tpo_chamfer_loss_fwd(int dtype, int flags, const void* xyz1, const void* xyz
   if (loss_uses_keys_kernel(dtype, B, N, M)) {
     // keys to the empty key and the reduction counters to 0xffffffff: one fill
     const size_t es = (size_t)dtype_size(dtype);
-    if ((s = fill_prefetch(w, L.kl + keys_loss_counter_bytes(B), nullptr, 0, 0xff, xyz1,
-                           es * 3 * B * N, xyz2, es * 3 * B * M, st)))
+    // ... and the gradient region to zero, in the same launch
+    if ((s = fill_prefetch(w, L.kl + keys_loss_counter_bytes(B), w + L.g1, L.total - L.g1, 0xff,
+                           xyz1, es * 3 * B * N, xyz2, es * 3 * B * M, st, 0)))
       return s;
     return chamfer_loss_keys(dtype, flags, xyz1, xyz2, B, N, M, reduction, k1, k2, w + L.kl, loss,
                              w + L.fin, st);
   }
   if (L.kl && (s = cuda_status(cudaMemsetAsync(w, 0xff, L.kl, st)))) return s;
   if ((s = cuda_status(cudaMemsetAsync(w + L.fin + kFinPartialBytes, 0xff, 256, st)))) return s;
+  if (L.total > L.g1 && (s = cuda_status(cudaMemsetAsync(w + L.g1, 0, L.total - L.g1, st)))) return s;
   if (B > 0 && N > 0 && M > 0 &&
       (s = chamfer_fwd_keys(dtype, flags, xyz1, xyz2, B, N, M, 0, N, k1, k2, st)))
     return s;
   return chamfer_finalize(dtype, flags, xyz1, xyz2, B, N, M, 0, N, k1, k2, nullptr,
                           (int32_t*)(w + L.idx1), nullptr, (int32_t*)(w + L.idx2), true, loss,
                           reduction, w + L.fin, st);
+}
+
+// The gradient scatter of the fused loss into (already zeroed) gradient buffers.
+static int loss_bwd_scatter(int dtype, int flags, const void* xyz1, const void* xyz2, int64_t B,
+                            int64_t N, int64_t M, int reduction, const char* w,
+                            const void* grad_loss, void* grad_xyz1, void* grad_xyz2, cudaStream_t st) {
+  const LossLayout L = loss_layout(dtype, B, N, M);
+  if (loss_uses_keys_kernel(dtype, B, N, M)) {
+    const size_t kb = (size_t)tpo_chamfer_key_bytes(dtype);
+    return chamfer_bwd_from_keys(dtype, flags, xyz1, xyz2, B, N, M, w,
+                                 w + align256(kb * (size_t)B * (size_t)N), grad_loss, reduction,
+                                 grad_xyz1, grad_xyz2, st);
+  }
+  return chamfer_bwd_accumulate(dtype, xyz1, xyz2, B, N, M, 0, N, 0, M,
+                                (const int32_t*)(w + L.idx1), (const int32_t*)(w + L.idx2),
+                                nullptr, nullptr, grad_loss,
+                                reduction == TPO_REDUCE_MEAN ? 1 : 2, grad_xyz1, grad_xyz2, st);
 }
 
 int tpo_chamfer_loss_bwd(int dtype, int flags, const void* xyz1, const void* xyz2, int64_t B,
@@ -251,18 +274,28 @@ int tpo_chamfer_loss_bwd(int dtype, int flags, const void* xyz1, const void* xyz
   if ((s = fill_prefetch(grad_xyz1, es * 3 * B * N, grad_xyz2, es * 3 * B * M, 0, nullptr, 0,
                          nullptr, 0, st)))
     return s;
+  return loss_bwd_scatter(dtype, flags, xyz1, xyz2, B, N, M, reduction, (const char*)workspace,
+                          grad_loss, grad_xyz1, grad_xyz2, st);
+}
+
+size_t tpo_chamfer_loss_grad_offset(int dtype, int64_t B, int64_t N, int64_t M, int which) {
+  if (!valid_dtype(dtype) || B < 0 || N < 0 || M < 0 || (which != 1 && which != 2)) return 0;
   const LossLayout L = loss_layout(dtype, B, N, M);
-  const char* w = (const char*)workspace;
-  if (loss_uses_keys_kernel(dtype, B, N, M)) {
-    const size_t kb = (size_t)tpo_chamfer_key_bytes(dtype);
-    return chamfer_bwd_from_keys(dtype, flags, xyz1, xyz2, B, N, M, w,
-                                     w + align256(kb * (size_t)B * (size_t)N), grad_loss,
-                                     reduction, grad_xyz1, grad_xyz2, st);
-  }
-  return chamfer_bwd_accumulate(dtype, xyz1, xyz2, B, N, M, 0, N, 0, M,
-                                (const int32_t*)(w + L.idx1), (const int32_t*)(w + L.idx2),
-                                nullptr, nullptr, grad_loss,
-                                reduction == TPO_REDUCE_MEAN ? 1 : 2, grad_xyz1, grad_xyz2, st);
+  return which == 1 ? L.g1 : L.g2;
+}
+
+int tpo_chamfer_loss_bwd_workspace(int dtype, int flags, const void* xyz1, const void* xyz2,
+                                   int64_t B, int64_t N, int64_t M, int reduction,
+                                   void* workspace, const void* grad_loss, void* stream) {
+  int s = check_chamfer_shape(dtype, xyz1, xyz2, B, N, M);
+  if (s) return s;
+  if (reduction != TPO_REDUCE_MEAN && reduction != TPO_REDUCE_SUM)
+    return fail(TPO_ERR_INVALID_ARGUMENT, "chamfer_loss_bwd_workspace: bad reduction");
+  if (!grad_loss || !workspace) return fail(TPO_ERR_INVALID_ARGUMENT, "chamfer_loss_bwd_workspace: null pointer");
+  const LossLayout L = loss_layout(dtype, B, N, M);
+  char* w = (char*)workspace;
+  return loss_bwd_scatter(dtype, flags, xyz1, xyz2, B, N, M, reduction, w, grad_loss, w + L.g1,
+                          w + L.g2, (cudaStream_t)stream);
 }
 
 static int check_knn(int dtype, const void* p1, const void* p2, int64_t N, int64_t P1, int64_t P2,

@@ -137,15 +137,16 @@ namespace tpo {
 // input arrays (prefetch.global.L2: no register result, nothing waits on it) so
 // that the next kernel's first touches of its inputs hit L2.
 __global__ void fill_prefetch_kernel(unsigned char* d0, size_t n0, unsigned char* d1, size_t n1,
-                                     unsigned v32, const char* p0, size_t m0, const char* p1,
-                                     size_t m1) {
+                                     unsigned v32a, unsigned v32b, const char* p0, size_t m0,
+                                     const char* p1, size_t m1) {
   const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   const size_t nth = (size_t)gridDim.x * blockDim.x;
-  const uint4 v = make_uint4(v32, v32, v32, v32);
   pdl_trigger();  // the (PDL-launched) consumer may be scheduled; it waits for this grid
   for (int r = 0; r < 2; ++r) {
     unsigned char* d = r ? d1 : d0;
     const size_t n = r ? n1 : n0;
+    const unsigned v32 = r ? v32b : v32a;
+    const uint4 v = make_uint4(v32, v32, v32, v32);
     if (!d || !n) continue;
     size_t head = (16 - ((uintptr_t)d & 15)) & 15;
     if (head > n) head = n;
@@ -165,14 +166,15 @@ __global__ void fill_prefetch_kernel(unsigned char* d0, size_t n0, unsigned char
 }
 
 int fill_prefetch(void* d0, size_t n0, void* d1, size_t n1, unsigned char value, const void* p0,
-                  size_t m0, const void* p1, size_t m1, cudaStream_t st) {
+                  size_t m0, const void* p1, size_t m1, cudaStream_t st, int value1) {
   const size_t work = std::max(n0 + n1, (m0 + m1) / 8);
   if (work == 0) return TPO_OK;
   const int threads = 256;
   const unsigned blocks = (unsigned)std::min<size_t>((work / 16 + threads - 1) / threads + 1, 148 * 4);
   const unsigned v32 = value * 0x01010101u;
+  const unsigned v32b = (value1 < 0 ? value : (unsigned char)value1) * 0x01010101u;
   fill_prefetch_kernel<<<blocks, threads, 0, st>>>((unsigned char*)d0, n0, (unsigned char*)d1, n1,
-                                                   v32, (const char*)p0, m0, (const char*)p1, m1);
+                                                   v32, v32b, (const char*)p0, m0, (const char*)p1, m1);
   return check_launch();
 }
 

@@ -140,6 +140,31 @@ std::tuple<at::Tensor, at::Tensor> chamfer_loss_backward(const at::Tensor& xyz1_
   return {gx1, gx2};
 }
 
+// First backward of a fused-loss forward: the gradients land in the zeroed region
+// of the forward's workspace and are returned as views of it (no fill launch).
+std::tuple<at::Tensor, at::Tensor> chamfer_loss_backward_in_state(const at::Tensor& xyz1_,
+                                                                  const at::Tensor& xyz2_,
+                                                                  const at::Tensor& state,
+                                                                  const at::Tensor& grad_loss,
+                                                                  int64_t reduction, int64_t flags) {
+  const c10::cuda::CUDAGuard g(xyz1_.device());
+  const at::Tensor xyz1 = xyz1_.contiguous(), xyz2 = xyz2_.contiguous();
+  const int64_t B = xyz1.size(0), N = xyz1.size(1), M = xyz2.size(1);
+  const int dt = to_dtype(xyz1);
+  TORCH_CHECK(state.numel() >= (int64_t)tpo_chamfer_loss_workspace_size(dt, B, N, M),
+              "chamfer_loss_backward: state does not belong to these inputs");
+  const at::Tensor gl = grad_loss.to(xyz1.scalar_type()).reshape({1}).contiguous();
+  ok(tpo_chamfer_loss_bwd_workspace(dt, (int)flags, xyz1.data_ptr(), xyz2.data_ptr(), B, N, M,
+                                    (int)reduction, state.data_ptr(), gl.data_ptr(), stream_of(xyz1)),
+     "chamfer_loss_backward");
+  const int64_t es = xyz1.element_size();
+  const int64_t o1 = (int64_t)tpo_chamfer_loss_grad_offset(dt, B, N, M, 1);
+  const int64_t o2 = (int64_t)tpo_chamfer_loss_grad_offset(dt, B, N, M, 2);
+  auto gx1 = state.narrow(0, o1, es * 3 * B * N).view(xyz1.scalar_type()).view({B, N, 3});
+  auto gx2 = state.narrow(0, o2, es * 3 * B * M).view(xyz1.scalar_type()).view({B, M, 3});
+  return {gx1, gx2};
+}
+
 // Autograd for the fused loss in C++ (no Python on the training-step path).
 class ChamferLossFn : public torch::autograd::Function<ChamferLossFn> {
  public:
@@ -151,6 +176,7 @@ class ChamferLossFn : public torch::autograd::Function<ChamferLossFn> {
     ctx->save_for_backward({xyz1, xyz2, std::get<1>(out)});
     ctx->saved_data["reduction"] = reduction;
     ctx->saved_data["flags"] = flags;
+    ctx->saved_data["grads_in_state"] = true;  // the state's gradient region is still zero
     ctx->mark_non_differentiable({std::get<1>(out)});
     ctx->set_materialize_grads(false);  // no zero-filled grad for the state output
     return {std::get<0>(out), std::get<1>(out)};
@@ -159,9 +185,14 @@ class ChamferLossFn : public torch::autograd::Function<ChamferLossFn> {
                                                  torch::autograd::variable_list grads) {
     auto saved = ctx->get_saved_variables();
     if (!grads[0].defined()) return {at::Tensor(), at::Tensor(), at::Tensor(), at::Tensor()};
-    auto g = chamfer_loss_backward(saved[0], saved[1], saved[2], grads[0],
-                                   ctx->saved_data["reduction"].toInt(),
-                                   ctx->saved_data["flags"].toInt());
+    const bool first = ctx->saved_data["grads_in_state"].toBool();
+    ctx->saved_data["grads_in_state"] = false;
+    auto g = first ? chamfer_loss_backward_in_state(saved[0], saved[1], saved[2], grads[0],
+                                                    ctx->saved_data["reduction"].toInt(),
+                                                    ctx->saved_data["flags"].toInt())
+                   : chamfer_loss_backward(saved[0], saved[1], saved[2], grads[0],
+                                           ctx->saved_data["reduction"].toInt(),
+                                           ctx->saved_data["flags"].toInt());
     return {std::get<0>(g), std::get<1>(g), at::Tensor(), at::Tensor()};
   }
 };

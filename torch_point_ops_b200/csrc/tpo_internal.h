@@ -60,10 +60,11 @@ int chamfer_bwd_from_keys(int dtype, int flags, const void* x1, const void* x2, 
                               int64_t M, const void* k1, const void* k2, const void* grad_loss,
                               int reduction, void* gx1, void* gx2, cudaStream_t st);
 
-// Fills [d0, d0+n0) and [d1, d1+n1) with `value` and prefetches the byte ranges
-// [p0, p0+m0), [p1, p1+m1) into L2, in one launch (null / zero-size parts skipped).
+// Fills [d0, d0+n0) with `value` and [d1, d1+n1) with `value1` (default: the
+// same) and prefetches the byte ranges [p0, p0+m0), [p1, p1+m1) into L2, in one
+// launch (null / zero-size parts skipped).
 int fill_prefetch(void* d0, size_t n0, void* d1, size_t n1, unsigned char value, const void* p0,
-                  size_t m0, const void* p1, size_t m1, cudaStream_t st);
+                  size_t m0, const void* p1, size_t m1, cudaStream_t st, int value1 = -1);
 
 // Reads (and optionally clears) the device-side error flags of this device.
 int device_error_flags(unsigned* out, bool clear);
