@@ -19,6 +19,7 @@ struct BwdOps<float> {
   __device__ static float two_g(float g) { return __fmul_rn(g, 2.0f); }
   __device__ static float term(float g2, float a, float b) { return __fmul_rn(g2, __fsub_rn(a, b)); }
   __device__ static void add(float* p, float v) { atomicAdd(p, v); }
+  __device__ static void add3(float* p, const float* v) { red_add3f(p, v[0], v[1], v[2]); }
   __device__ static float neg(float v) { return -v; }
   __device__ static float div(float g, int64_t n) { return __fdiv_rn(g, (float)n); }
 };
@@ -27,6 +28,11 @@ struct BwdOps<double> {
   __device__ static double two_g(double g) { return __dmul_rn(g, 2.0); }
   __device__ static double term(double g2, double a, double b) { return __dmul_rn(g2, __dsub_rn(a, b)); }
   __device__ static void add(double* p, double v) { atomicAdd(p, v); }
+  __device__ static void add3(double* p, const double* v) {
+    atomicAdd(p, v[0]);
+    atomicAdd(p + 1, v[1]);
+    atomicAdd(p + 2, v[2]);
+  }
   __device__ static double neg(double v) { return -v; }
   __device__ static double div(double g, int64_t n) { return __ddiv_rn(g, (double)n); }
 };
@@ -35,6 +41,7 @@ struct BwdOps<__half> {
   __device__ static __half two_g(__half g) { return hmul_rn(g, __float2half_rn(2.0f)); }
   __device__ static __half term(__half g2, __half a, __half b) { return hmul_rn(g2, hsub_rn(a, b)); }
   __device__ static void add(__half* p, __half v) { atomicAdd(p, v); }
+  __device__ static void add3(__half* p, const __half* v) { red_add3h(p, v[0], v[1], v[2]); }
   __device__ static __half neg(__half v) { return __hneg(v); }
   __device__ static __half div(__half g, int64_t n) { return __float2half_rn(__half2float(g) / (float)n); }
 };
@@ -85,12 +92,14 @@ __global__ void chamfer_bwd_kernel(const T* __restrict__ x1, const T* __restrict
       g = scalar_mode ? gs2 : g2[o];
     }
     const T gg = O::two_g(g);
+    T v[3], nv[3];
 #pragma unroll
     for (int d = 0; d < 3; ++d) {
-      const T v = O::term(gg, pa[d], pb[d]);
-      O::add(ga + d, v);
-      O::add(gb + d, O::neg(v));
+      v[d] = O::term(gg, pa[d], pb[d]);
+      nv[d] = O::neg(v[d]);
     }
+    O::add3(ga, v);
+    O::add3(gb, nv);
   }
 }
 

@@ -868,6 +868,7 @@ struct FkOps<float> {
   }
   __device__ static float term(float g, float a, float b) { return __fmul_rn(g, __fsub_rn(a, b)); }
   __device__ static void add(float* p, float v) { atomicAdd(p, v); }
+  __device__ static void add3(float* p, const float* v) { red_add3f(p, v[0], v[1], v[2]); }
   __device__ static float neg(float v) { return -v; }
 };
 template <>
@@ -878,6 +879,7 @@ struct FkOps<__half> {
   }
   __device__ static __half term(__half g, __half a, __half b) { return hmul_rn(g, hsub_rn(a, b)); }
   __device__ static void add(__half* p, __half v) { atomicAdd(p, v); }
+  __device__ static void add3(__half* p, const __half* v) { red_add3h(p, v[0], v[1], v[2]); }
   __device__ static __half neg(__half v) { return __hneg(v); }
 };
 
@@ -914,12 +916,14 @@ __global__ void chamfer_bwd_from_keys_kernel(const T* __restrict__ xyz1, const T
     T* ga = (row ? gx1 : gx2) + u * 3;
     T* gb = (row ? gx2 : gx1) + (b * Q + j) * 3;
     const T* pb = other + (int64_t)j * 3;
+    T v[3], nv[3];
 #pragma unroll
     for (int d = 0; d < 3; ++d) {
-      const T v = O::term(gg, q[d], pb[d]);
-      O::add(ga + d, v);
-      O::add(gb + d, O::neg(v));
+      v[d] = O::term(gg, q[d], pb[d]);
+      nv[d] = O::neg(v[d]);
     }
+    O::add3(ga, v);
+    O::add3(gb, nv);
   }
 }
 

@@ -449,6 +449,7 @@ struct KbOps<float> {
   __device__ static float l1(float g, float a, float b) { return a > b ? g : (a == b ? 0.0f : -g); }
   __device__ static float add(float a, float b) { return __fadd_rn(a, b); }
   __device__ static void atomic_sub(float* p, float v) { atomicAdd(p, -v); }
+  __device__ static void atomic_sub3(float* p, const float* v) { red_add3f(p, -v[0], -v[1], -v[2]); }
   __device__ static float zero() { return 0.0f; }
 };
 template <>
@@ -457,6 +458,11 @@ struct KbOps<double> {
   __device__ static double l1(double g, double a, double b) { return a > b ? g : (a == b ? 0.0 : -g); }
   __device__ static double add(double a, double b) { return __dadd_rn(a, b); }
   __device__ static void atomic_sub(double* p, double v) { atomicAdd(p, -v); }
+  __device__ static void atomic_sub3(double* p, const double* v) {
+    atomicAdd(p, -v[0]);
+    atomicAdd(p + 1, -v[1]);
+    atomicAdd(p + 2, -v[2]);
+  }
   __device__ static double zero() { return 0.0; }
 };
 template <>
@@ -470,6 +476,9 @@ struct KbOps<__half> {
   }
   __device__ static __half add(__half a, __half b) { return hadd_rn(a, b); }
   __device__ static void atomic_sub(__half* p, __half v) { atomicAdd(p, __hneg(v)); }
+  __device__ static void atomic_sub3(__half* p, const __half* v) {
+    red_add3h(p, __hneg(v[0]), __hneg(v[1]), __hneg(v[2]));
+  }
   __device__ static __half zero() { return __float2half_rn(0.0f); }
 };
 
@@ -513,6 +522,17 @@ __global__ void knn_bwd_kernel(const T* __restrict__ p1, const T* __restrict__ p
         const int64_t j = idxs[t * K + k];
         if (j < 0 || j >= P2) continue;
         const T g = gd[t * K + k];
+        if (D == 3) {  // one vector reduction + one scalar for the neighbour's 3 components
+          T v[3];
+#pragma unroll
+          for (int d = 0; d < 3; ++d) {
+            const T a = p1[t * 3 + d], b = p2[(n * P2 + j) * 3 + d];
+            v[d] = norm == 1 ? O::l1(g, a, b) : O::l2(g, a, b);
+            acc[d] = O::add(acc[d], v[d]);
+          }
+          O::atomic_sub3(g2 + (n * P2 + j) * 3, v);
+          continue;
+        }
 #pragma unroll
         for (int d = 0; d < KDMAX; ++d) {
           if (d < D) {

@@ -241,6 +241,34 @@ __device__ __forceinline__ bool mbar_wait(unsigned long long* bar, unsigned pari
   return false;
 }
 
+// Atomic add of a 3-vector of floats at p (4-byte aligned, as in an (n,3) array):
+// one 8-byte vector reduction for the aligned pair plus one scalar, instead of
+// three scalar reductions.  Each component is added (and rounded) on its own.
+__device__ __forceinline__ void red_add_v2f(float* p, float a, float b) {
+  asm volatile("red.global.add.v2.f32 [%0], {%1, %2};" ::"l"(p), "f"(a), "f"(b) : "memory");
+}
+__device__ __forceinline__ void red_add3f(float* p, float x, float y, float z) {
+  if ((reinterpret_cast<uintptr_t>(p) & 7) == 0) {
+    red_add_v2f(p, x, y);
+    atomicAdd(p + 2, z);
+  } else {
+    atomicAdd(p, x);
+    red_add_v2f(p + 1, y, z);
+  }
+}
+
+// The same for a 3-vector of halves (2-byte aligned): one packed half2 atomic for
+// the 4-byte aligned pair plus one scalar.
+__device__ __forceinline__ void red_add3h(__half* p, __half x, __half y, __half z) {
+  if ((reinterpret_cast<uintptr_t>(p) & 3) == 0) {
+    atomicAdd(reinterpret_cast<__half2*>(p), __halves2half2(x, y));
+    atomicAdd(p + 2, z);
+  } else {
+    atomicAdd(p, x);
+    atomicAdd(reinterpret_cast<__half2*>(p + 1), __halves2half2(y, z));
+  }
+}
+
 // Programmatic dependent launch.  A kernel launched with launch_pdl may start
 // while the previous kernel in the stream is still running; it must call
 // pdl_wait() before touching global memory (that returns once the previous
