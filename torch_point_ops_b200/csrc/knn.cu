@@ -573,70 +573,111 @@ int knn_backward(int dtype, const void* p1, const void* p2, const int64_t* l1, c
 
 // ------------------------------- knn_gather -------------------------------
 // out[n,l,k,u] = x[n, idx[n,l,k], u]; zero when k >= lengths[n] or idx invalid.
-template <typename T>
+// One thread per (n, l, k) slot, all U features of it; index math in IdxT
+// (32-bit whenever N*L*K and the element offsets fit).
+template <typename T, typename IdxT>
 __global__ void knn_gather_fwd_kernel(const T* __restrict__ x, const int64_t* __restrict__ idx,
-                                      const int64_t* __restrict__ lengths, int64_t N, int64_t M,
-                                      int64_t U, int64_t L, int64_t K, T* __restrict__ out) {
-  const int64_t total = N * L * K * U;
-  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total;
-       t += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t u = t % U;
-    const int64_t e = t / U;  // (n, l, k)
-    const int64_t k = e % K;
-    const int64_t n = e / (L * K);
-    const int64_t len = lengths ? lengths[n] : M;
+                                      const int64_t* __restrict__ lengths, IdxT N, IdxT M, IdxT U,
+                                      IdxT L, IdxT K, T* __restrict__ out) {
+  const IdxT slots = N * L * K;
+  for (IdxT e = blockIdx.x * (IdxT)blockDim.x + threadIdx.x; e < slots;
+       e += (IdxT)gridDim.x * blockDim.x) {
+    const IdxT k = e % K;
+    const IdxT n = e / (L * K);
+    const int64_t len = lengths ? lengths[n] : (int64_t)M;
     const int64_t j = idx[e];
-    out[t] = (k < len && j >= 0 && j < M) ? x[(n * M + j) * U + u] : T(0.0f);
+    const bool ok = k < len && j >= 0 && j < (int64_t)M;
+    const T* src = x + ((int64_t)n * M + (ok ? j : 0)) * U;
+    T* dst = out + (int64_t)e * U;
+    for (IdxT u = 0; u < U; ++u) dst[u] = ok ? src[u] : T(0.0f);
   }
 }
 
 template <typename T>
+__device__ __forceinline__ void gather_add3(T* p, const T* v);
+template <>
+__device__ __forceinline__ void gather_add3<float>(float* p, const float* v) { red_add3f(p, v[0], v[1], v[2]); }
+template <>
+__device__ __forceinline__ void gather_add3<__half>(__half* p, const __half* v) { red_add3h(p, v[0], v[1], v[2]); }
+template <>
+__device__ __forceinline__ void gather_add3<double>(double* p, const double* v) {
+  atomicAdd(p, v[0]);
+  atomicAdd(p + 1, v[1]);
+  atomicAdd(p + 2, v[2]);
+}
+
+template <typename T, typename IdxT>
 __global__ void knn_gather_bwd_kernel(const T* __restrict__ gout, const int64_t* __restrict__ idx,
-                                      const int64_t* __restrict__ lengths, int64_t N, int64_t M,
-                                      int64_t U, int64_t L, int64_t K, T* __restrict__ gx) {
-  const int64_t total = N * L * K * U;
-  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total;
-       t += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t u = t % U;
-    const int64_t e = t / U;
-    const int64_t k = e % K;
-    const int64_t n = e / (L * K);
-    const int64_t len = lengths ? lengths[n] : M;
+                                      const int64_t* __restrict__ lengths, IdxT N, IdxT M, IdxT U,
+                                      IdxT L, IdxT K, T* __restrict__ gx) {
+  const IdxT slots = N * L * K;
+  for (IdxT e = blockIdx.x * (IdxT)blockDim.x + threadIdx.x; e < slots;
+       e += (IdxT)gridDim.x * blockDim.x) {
+    const IdxT k = e % K;
+    const IdxT n = e / (L * K);
+    const int64_t len = lengths ? lengths[n] : (int64_t)M;
     const int64_t j = idx[e];
-    if (k < len && j >= 0 && j < M) atomicAdd(gx + (n * M + j) * U + u, gout[t]);
+    if (!(k < len && j >= 0 && j < (int64_t)M)) continue;
+    T* dst = gx + ((int64_t)n * M + j) * U;
+    const T* src = gout + (int64_t)e * U;
+    if (U == 3) {
+      const T v[3] = {src[0], src[1], src[2]};
+      gather_add3<T>(dst, v);
+    } else {
+      for (IdxT u = 0; u < U; ++u) atomicAdd(dst + u, src[u]);
+    }
   }
+}
+
+template <typename T, typename IdxT>
+static void launch_gather(bool bwd, const void* a, const int64_t* idx, const int64_t* lengths,
+                          int64_t N, int64_t M, int64_t U, int64_t L, int64_t K, void* out,
+                          cudaStream_t st) {
+  const int64_t slots = N * L * K;
+  const int threads = 256;
+  const unsigned blocks = (unsigned)std::min<int64_t>((slots + threads - 1) / threads, 148 * 16);
+  if (bwd)
+    knn_gather_bwd_kernel<T, IdxT><<<blocks, threads, 0, st>>>((const T*)a, idx, lengths, (IdxT)N, (IdxT)M,
+                                                               (IdxT)U, (IdxT)L, (IdxT)K, (T*)out);
+  else
+    knn_gather_fwd_kernel<T, IdxT><<<blocks, threads, 0, st>>>((const T*)a, idx, lengths, (IdxT)N, (IdxT)M,
+                                                               (IdxT)U, (IdxT)L, (IdxT)K, (T*)out);
+}
+
+static int gather_dispatch(bool bwd, int dtype, const void* a, const int64_t* idx,
+                           const int64_t* lengths, int64_t N, int64_t M, int64_t U, int64_t L,
+                           int64_t K, void* out, cudaStream_t st) {
+  if (N * L * K <= 0 || U <= 0) return TPO_OK;
+  // 32-bit index math when every slot index and slot-count product fits
+  const bool small = N * L * K < (int64_t(1) << 31) && N * M < (int64_t(1) << 31);
+  switch (dtype) {
+    case TPO_F32:
+      small ? launch_gather<float, int>(bwd, a, idx, lengths, N, M, U, L, K, out, st)
+            : launch_gather<float, int64_t>(bwd, a, idx, lengths, N, M, U, L, K, out, st);
+      break;
+    case TPO_F16:
+      small ? launch_gather<__half, int>(bwd, a, idx, lengths, N, M, U, L, K, out, st)
+            : launch_gather<__half, int64_t>(bwd, a, idx, lengths, N, M, U, L, K, out, st);
+      break;
+    case TPO_F64:
+      small ? launch_gather<double, int>(bwd, a, idx, lengths, N, M, U, L, K, out, st)
+            : launch_gather<double, int64_t>(bwd, a, idx, lengths, N, M, U, L, K, out, st);
+      break;
+    default: return TPO_ERR_INVALID_ARGUMENT;
+  }
+  return check_launch();
 }
 
 int knn_gather_forward(int dtype, const void* x, const int64_t* idx, const int64_t* lengths,
                        int64_t N, int64_t M, int64_t U, int64_t L, int64_t K, void* out,
                        cudaStream_t st) {
-  const int64_t total = N * L * K * U;
-  if (total <= 0) return TPO_OK;
-  const int threads = 256;
-  const unsigned blocks = (unsigned)std::min<int64_t>((total + threads - 1) / threads, 148 * 16);
-  switch (dtype) {
-    case TPO_F32: knn_gather_fwd_kernel<float><<<blocks, threads, 0, st>>>((const float*)x, idx, lengths, N, M, U, L, K, (float*)out); break;
-    case TPO_F16: knn_gather_fwd_kernel<__half><<<blocks, threads, 0, st>>>((const __half*)x, idx, lengths, N, M, U, L, K, (__half*)out); break;
-    case TPO_F64: knn_gather_fwd_kernel<double><<<blocks, threads, 0, st>>>((const double*)x, idx, lengths, N, M, U, L, K, (double*)out); break;
-    default: return TPO_ERR_INVALID_ARGUMENT;
-  }
-  return check_launch();
+  return gather_dispatch(false, dtype, x, idx, lengths, N, M, U, L, K, out, st);
 }
 
 int knn_gather_backward(int dtype, const void* gout, const int64_t* idx, const int64_t* lengths,
                         int64_t N, int64_t M, int64_t U, int64_t L, int64_t K, void* gx,
                         cudaStream_t st) {
-  const int64_t total = N * L * K * U;
-  if (total <= 0) return TPO_OK;
-  const int threads = 256;
-  const unsigned blocks = (unsigned)std::min<int64_t>((total + threads - 1) / threads, 148 * 16);
-  switch (dtype) {
-    case TPO_F32: knn_gather_bwd_kernel<float><<<blocks, threads, 0, st>>>((const float*)gout, idx, lengths, N, M, U, L, K, (float*)gx); break;
-    case TPO_F16: knn_gather_bwd_kernel<__half><<<blocks, threads, 0, st>>>((const __half*)gout, idx, lengths, N, M, U, L, K, (__half*)gx); break;
-    case TPO_F64: knn_gather_bwd_kernel<double><<<blocks, threads, 0, st>>>((const double*)gout, idx, lengths, N, M, U, L, K, (double*)gx); break;
-    default: return TPO_ERR_INVALID_ARGUMENT;
-  }
-  return check_launch();
+  return gather_dispatch(true, dtype, gout, idx, lengths, N, M, U, L, K, gx, st);
 }
 
 }  // namespace tpo
