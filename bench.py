@@ -299,6 +299,15 @@ def run_ours(args, cfg):
     # ---- e2e through the public API with pinned host buffers ----
     e2e = run_e2e(args, cfg, step, host_inputs, dev, flush, ws)
     e2e_value = pairs * jobs / (e2e["ms"] * 1e-3) / 1e9
+    e2e_pipe = run_e2e_pipelined(args, cfg, step, host_inputs, dev, ws)
+    e2e_pipe_value = pairs * jobs / (e2e_pipe["ms"] * 1e-3) / 1e9
+    e2e_graph = None
+    if not sharded:  # the sharded step runs NCCL collectives: not captured
+        try:
+            e2e_graph = run_e2e_pipelined(args, cfg, step, host_inputs, dev, ws, graphs=True)
+        except Exception as e:  # capture unsupported -> reported as absent
+            print(f"[bench] e2e graph capture failed ({e})", file=sys.stderr)
+    e2e_graph_value = pairs * jobs / (e2e_graph["ms"] * 1e-3) / 1e9 if e2e_graph else None
 
     # ---- the dominant kernel alone, for the roofline ----
     rows = None
@@ -309,7 +318,9 @@ def run_ours(args, cfg):
     roof_bwd = None if sharded else bwd_roofline(cfg, inputs, dev)
     return dict(roofline_bwd=roof_bwd, value=value, ms_per_step=ms_per_step, pairs=pairs, graph=graph is not None,
                 sharded=sharded,
-                clocks=clk.summary(), e2e=e2e, e2e_value=e2e_value, roofline=roof)
+                clocks=clk.summary(), e2e=e2e, e2e_value=e2e_value, e2e_pipe=e2e_pipe,
+                e2e_pipe_value=e2e_pipe_value, e2e_graph=e2e_graph, e2e_graph_value=e2e_graph_value,
+                roofline=roof)
 
 
 def run_e2e(args, cfg, step, host_inputs, dev, flush, ws):
@@ -347,6 +358,95 @@ def run_e2e(args, cfg, step, host_inputs, dev, flush, ws):
         tot = float(t.item())
     bo = sum(h.numel() * h.element_size() for h in outs_host)
     return {"ms": tot / args.steps, "h2d": hi_bytes, "d2h": bo}
+
+
+def run_e2e_pipelined(args, cfg, step, host_inputs, dev, ws, graphs=False):
+    """The same public-API step and the same per-step copies as run_e2e, issued
+    the way a training input pipeline runs them: step i's host->device input copy
+    (pinned, its own stream) overlaps step i-1's compute, and step i's
+    device->host result copy (third stream, from a device staging buffer the
+    compute stream fills) overlaps step i+1's compute.  Two device input
+    buffers, two staging buffers and two pinned output buffers rotate; every
+    step still copies all of its inputs in and all of its results out inside
+    the timed region, which spans K steps end to end (max over ranks).  With
+    graphs=True the compute stage of each buffer set (API step + staging copy)
+    is a captured CUDA graph, so the host issues only copies and replays."""
+    pinned = [t.pin_memory() for t in host_inputs]
+    s_in, s_cmp, s_out = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
+    nb = 2
+    dbuf = [[torch.empty(t.shape, dtype=t.dtype, device=dev) for t in pinned] for _ in range(nb)]
+    xsb = [[d.requires_grad_() if d.is_floating_point() and cfg["kind"] != "fps" else d for d in db]
+           for db in dbuf]
+    dout = [None] * nb  # results staged on the compute stream, read by the D2H stream
+    hout = [None] * nb
+    ev_in = [torch.cuda.Event() for _ in range(nb)]
+    ev_used = [torch.cuda.Event() for _ in range(nb)]
+    ev_out = [torch.cuda.Event() for _ in range(nb)]
+
+    def compute(b):
+        outs = [o.detach() for o in step(*xsb[b])]
+        if dout[b] is None:
+            dout[b] = [torch.empty(o.shape, dtype=o.dtype, device=dev) for o in outs]
+        for d, o in zip(dout[b], outs):
+            d.copy_(o)
+
+    gr = [None] * nb
+    with torch.cuda.stream(s_cmp):
+        for b in range(nb):
+            for _ in range(3):
+                compute(b)
+    torch.cuda.synchronize()
+    if graphs:
+        for b in range(nb):
+            gr[b] = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr[b]):
+                compute(b)
+    hout = [[torch.empty(d.shape, dtype=d.dtype, pin_memory=True) for d in dout[b]] for b in range(nb)]
+    state = {"i": 0}
+
+    def issue():
+        i = state["i"]
+        b = i % nb
+        state["i"] = i + 1
+        with torch.cuda.stream(s_in):
+            if i >= nb:
+                s_in.wait_event(ev_used[b])  # the compute that read dbuf[b] is done
+            with torch.no_grad():
+                for d, h in zip(dbuf[b], pinned):
+                    d.copy_(h, non_blocking=True)
+            ev_in[b].record(s_in)
+        with torch.cuda.stream(s_cmp):
+            s_cmp.wait_event(ev_in[b])
+            if i >= nb:
+                s_cmp.wait_event(ev_out[b])  # the D2H that read dout[b] is done
+            if graphs:
+                gr[b].replay()
+            else:
+                compute(b)
+            ev_used[b].record(s_cmp)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev_used[b])
+            for h, d in zip(hout[b], dout[b]):
+                h.copy_(d, non_blocking=True)
+            ev_out[b].record(s_out)
+
+    for _ in range(max(3, args.warmup)):
+        issue()
+    torch.cuda.synchronize()
+    if ws > 1:
+        torch.distributed.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(s_in)
+    for _ in range(args.steps):
+        issue()
+    end.record(s_out)
+    end.synchronize()
+    tot = start.elapsed_time(end)
+    if ws > 1:
+        t = torch.tensor([tot], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        tot = float(t.item())
+    return {"ms": tot / args.steps}
 
 
 def kernel_roofline(cfg, inputs, dev, clocks, reps=20, rows=None):
@@ -740,6 +840,30 @@ def run_reference(args, cfg):
     return line
 
 
+def e2e_line(cfg, r):
+    """The e2e object: the best of the measured end-to-end modes (all run the
+    public API with every step's H2D inputs and D2H results inside the timed
+    region), with each mode's number beside it."""
+    modes = {
+        "pipelined": (r["e2e_pipe_value"], r["e2e_pipe"]["ms"],
+                      "eager API call; step i's H2D (pinned, own stream) overlaps step i-1's compute, "
+                      "its D2H overlaps step i+1's; K-step span"),
+        "serial": (r["e2e_value"], r["e2e"]["ms"],
+                   "eager API call; H2D, step, D2H back to back per step, L2 flushed before each"),
+    }
+    if r.get("e2e_graph_value"):
+        modes["pipelined_graph"] = (r["e2e_graph_value"], r["e2e_graph"]["ms"],
+                                    "as pipelined, with each buffer set's API step captured as a "
+                                    "CUDA graph (copies issued per step on their own streams)")
+    best = max(modes, key=lambda k: modes[k][0])
+    out = {"value": round(modes[best][0], 2), "unit": unit_of(cfg),
+           "h2d_bytes_per_step": r["e2e"]["h2d"], "d2h_bytes_per_step": r["e2e"]["d2h"],
+           "ms_per_step": round(modes[best][1], 4), "mode": best,
+           "modes": {k: {"value": round(v[0], 2), "ms_per_step": round(v[1], 4), "how": v[2]}
+                     for k, v in modes.items()}}
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -785,9 +909,7 @@ def main():
                                    if r["sharded"] else f"dp{ws} (independent batch per GPU)"),
                    "cuda_graph": r["graph"]},
         "clocks": r["clocks"],
-        "e2e": {"value": round(r["e2e_value"], 2), "unit": unit_of(cfg),
-                "h2d_bytes_per_step": r["e2e"]["h2d"], "d2h_bytes_per_step": r["e2e"]["d2h"],
-                "ms_per_step": round(r["e2e"]["ms"], 4)},
+        "e2e": e2e_line(cfg, r),
         "gpu_launches": launches_per_step(cfg) * args.steps,
         "roofline": r["roofline"],
         "roofline_bwd": r["roofline_bwd"],
