@@ -17,8 +17,14 @@ max-reduced.  Rank 0 prints one JSON line.
 
 `value` = device-resident throughput (inputs already in HBM; the step is a CUDA
 graph of the public API's forward + backward).  `e2e` = the same metric through
-the public API (ChamferDistance / knn_points) with pinned HOST inputs: H2D copy,
-forward, backward and D2H of loss + gradients inside the timed region.
+the public API (ChamferDistance / knn_points / furthest_point_sampling) with
+pinned HOST inputs: every step's H2D copy, forward, backward and D2H of loss +
+gradients inside the timed region; the best of three issue modes (serial,
+pipelined copies on their own streams, pipelined with graph-captured steps),
+each listed under e2e.modes.
+
+Other configs: 1, 3, 4 (knn), 5 / 5d (one 2^20-point cloud pair, row-sharded
+over the GPUs when N > 1), 2h (fp16), fps / fpsb (furthest point sampling).
 """
 from __future__ import annotations
 
