@@ -156,3 +156,58 @@ def test_gather_points_autograd_and_errors():
     # empty gathers
     e = tpo.gather_points(pts, idx[:, :0])
     assert e.shape == (2, 4, 0)
+
+
+def test_fps_opcheck_and_compile():
+    """torch.library.opcheck on the fps / gather_points operators and torch.compile
+    of the public functions (the reference's tests/test_fps.py test_opcheck /
+    test_compile)."""
+    pts = torch.randn(1, 10, 3, device=DEV)
+    feats = torch.randn(1, 4, 10, device=DEV)
+    idx = torch.tensor([[0, 2, 4, 6]], device=DEV)
+    torch.library.opcheck(torch.ops.torch_point_ops_b200_fps.fps_forward.default, (pts, 4),
+                          raise_exception=True)
+    torch.library.opcheck(torch.ops.torch_point_ops_b200_fps.gather_points_forward.default,
+                          (feats, idx), raise_exception=True)
+    gout = torch.randn(1, 4, 4, device=DEV)
+    torch.library.opcheck(torch.ops.torch_point_ops_b200_fps.gather_points_backward.default,
+                          (gout, idx, 10), raise_exception=True)
+    p20 = torch.randn(1, 20, 3, device=DEV)
+    eager = tpo.furthest_point_sampling(p20, 8)
+    compiled = torch.compile(tpo.furthest_point_sampling)(p20, 8)
+    assert torch.equal(eager, compiled)
+    f20 = torch.randn(1, 6, 20, device=DEV)
+    assert torch.equal(torch.compile(tpo.gather_points)(f20, eager), tpo.gather_points(f20, eager))
+
+
+def test_fps_known_grid_and_degenerate():
+    """A 5x5 grid in the z=0 plane (the reference's test_known_configurations): the
+    centre point sits at the origin, so it is degenerate and never chosen; and
+    points placed at 1e-4 (test_degenerate_points) are never chosen either."""
+    x = torch.linspace(-1, 1, 5)
+    xx, yy = torch.meshgrid(x, x, indexing="ij")
+    grid = torch.stack([xx.flatten(), yy.flatten(), torch.zeros(25)], dim=-1)[None]
+    idx = tpo.furthest_point_sampling(grid.to(DEV), 5).cpu()
+    np.testing.assert_array_equal(idx.numpy(), oracle.fps(grid.numpy(), 5))
+    assert idx[0, 0] == 0 and len(torch.unique(idx[0])) == 5 and 12 not in idx[0].tolist()
+    g = torch.Generator().manual_seed(5)
+    p = torch.randn(1, 10, 3, generator=g)
+    p[0, 5:8] = 1e-4
+    idx = tpo.furthest_point_sampling(p.to(DEV), 5).cpu()
+    np.testing.assert_array_equal(idx.numpy(), oracle.fps(p.numpy(), 5))
+    assert not set(idx[0].tolist()) & {5, 6, 7}
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32, torch.float64])
+def test_fps_gather_multi_precision(dtype):
+    """fps + gather_points keep the input dtype; gradients flow in every dtype
+    (the reference's test_multi_precision)."""
+    g = torch.Generator().manual_seed(6)
+    pts = torch.randn(1, 50, 3, generator=g).to(dtype).to(DEV)
+    feats = torch.randn(1, 4, 50, generator=g).to(dtype).to(DEV).requires_grad_()
+    idx = tpo.furthest_point_sampling(pts, 8)
+    np.testing.assert_array_equal(idx.cpu().numpy(), oracle.fps(pts.cpu().numpy(), 8))
+    out = tpo.gather_points(feats, idx)
+    assert out.dtype == dtype and out.shape == (1, 4, 8)
+    out.sum().backward()
+    assert feats.grad.dtype == dtype and float(feats.grad.float().sum()) == 4 * 8
