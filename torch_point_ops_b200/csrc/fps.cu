@@ -34,6 +34,10 @@
 //  * if no point is valid the step selects 0 (besti's initial value, fps.cu:131).
 #include <cooperative_groups.h>
 
+#include <map>
+#include <mutex>
+#include <tuple>
+
 #include <type_traits>
 
 #include "tpo_internal.h"
@@ -208,6 +212,7 @@ __device__ __forceinline__ int fps_rank_to_index(int r, int P, int bs, int lbs, 
 constexpr unsigned kFpsWaitLimit = 1u << 22;
 constexpr int kFpsMaxThreads = 256;
 constexpr int kFpsMaxCluster = 16;
+constexpr int kFpsSmemCap = 200 * 1024;  // dynamic shared memory limit of every plan
 
 enum FpsMode { kFpsCta = 0, kFpsCluster = 1, kFpsGrid = 2 };
 
@@ -543,7 +548,7 @@ static int fps_cluster_capacity(int G, int NT, int PT, int* out) {
   void* fn = fps_kernel_for<Tr>(kFpsCluster, PT);
   if (!fn) return TPO_ERR_UNSUPPORTED;
   const size_t smem = fps_smem_bytes<Tr>(kFpsCluster, G, NT, PT);
-  if (int s = cuda_status(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)))
+  if (int s = cuda_status(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kFpsSmemCap)))
     return s;
   if (G > 8)
     if (int s = cuda_status(cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1)))
@@ -577,7 +582,34 @@ static double fps_step_cycles(int dtype, int mode, int G, int NT, int PT) {
 }
 
 template <class Tr>
+static int fps_plan_uncached(int dtype, int64_t B, int64_t P, FpsPlan* plan);
+
+// Plans are cached per (device, dtype, B, P): planning queries the occupancy
+// calculator and sets kernel attributes, which costs more than a small launch.
+template <class Tr>
 static int fps_plan(int dtype, int64_t B, int64_t P, FpsPlan* plan) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int64_t, int64_t>, FpsPlan> cache;
+  int dev = 0;
+  if (int s = cuda_status(cudaGetDevice(&dev))) return s;
+  const auto key = std::make_tuple(dev, dtype, B, P);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+      *plan = it->second;
+      return TPO_OK;
+    }
+  }
+  if (int s = fps_plan_uncached<Tr>(dtype, B, P, plan)) return s;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache.size() > 4096) cache.clear();
+  cache[key] = *plan;
+  return TPO_OK;
+}
+
+template <class Tr>
+static int fps_plan_uncached(int dtype, int64_t B, int64_t P, FpsPlan* plan) {
   if (!g_num_sms) {
     int dev = 0;
     if (int s = cuda_status(cudaGetDevice(&dev))) return s;
@@ -596,7 +628,7 @@ static int fps_plan(int dtype, int64_t B, int64_t P, FpsPlan* plan) {
           if ((int64_t)G * NT * PT < Pv) continue;
           // smallest PT that covers the cloud for this (G, NT)
           if (PT > 2 && (int64_t)G * NT * (PT / 2) >= Pv) continue;
-          if (fps_smem_bytes<Tr>(mode, G, NT, PT) > 200 * 1024) continue;
+          if (fps_smem_bytes<Tr>(mode, G, NT, PT) > (size_t)kFpsSmemCap) continue;
           // concurrent groups (one CTA per SM assumed for G > 1)
           int64_t per_wave = mode == kFpsCta ? (int64_t)sms * std::max(1, 1024 / NT) : sms / G;
           if (per_wave < 1) continue;
@@ -640,7 +672,9 @@ static int fps_run(int dtype, const void* pts, int64_t B, int64_t P, int64_t S, 
   if (need > ws_bytes) return set_error(TPO_ERR_WORKSPACE, "fps: workspace too small");
   void* fn = fps_kernel_for<Tr>(p.mode, p.PT);
   const size_t smem = fps_smem_bytes<Tr>(p.mode, p.G, p.NT, p.PT);
-  if (int s = cuda_status(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)))
+  // one fixed cap for every plan (plans need at most kFpsSmemCap): concurrent
+  // callers with different plans never lower each other's limit
+  if (int s = cuda_status(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kFpsSmemCap)))
     return s;
   unsigned* gcount = nullptr;
   typename Tr::Slot* gslots = nullptr;
