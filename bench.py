@@ -18,10 +18,12 @@ max-reduced.  Rank 0 prints one JSON line.
 `value` = device-resident throughput (inputs already in HBM; the step is a CUDA
 graph of the public API's forward + backward).  `e2e` = the same metric through
 the public API (ChamferDistance / knn_points / furthest_point_sampling) with
-pinned HOST inputs: every step's H2D copy, forward, backward and D2H of loss +
-gradients inside the timed region; the best of three issue modes (serial,
-pipelined copies on their own streams, pipelined with graph-captured steps),
-each listed under e2e.modes.
+pinned HOST inputs: every step's H2D copy (the step's inputs packed in one
+pinned buffer), forward, backward and the D2H read of the step's result (the
+loss; fps: the sampled indices) inside the timed region; the best of three
+issue modes (serial, pipelined copies on their own streams, pipelined with
+graph-captured steps), each listed under e2e.modes, plus the pipelined number
+with every gradient also read back (e2e.with_gradient_readback).
 
 Other configs: 1, 3, 4 (knn), 5 / 5d (one 2^20-point cloud pair, row-sharded
 over the GPUs when N > 1), 2h (fp16), fps / fpsb (furthest point sampling).
@@ -219,9 +221,10 @@ def step_fn(cfg, sharded=False):
 
 
 def launches_per_step(cfg):
-    # chamfer: fill, keys, loss reduction (fwd), fill + scatter (bwd); knn: knn
-    # fwd, gather fwd, gather bwd, knn bwd; fps: one sampling kernel
-    return {"chamfer": 5, "knn": 4, "fps": 1}[cfg["kind"]]
+    # chamfer: fill, keys, loss reduction (fwd), gradient scatter into the
+    # forward's zero-filled workspace (bwd); knn: knn fwd, gather fwd, gather
+    # bwd, knn bwd; fps: one sampling kernel
+    return {"chamfer": 4, "knn": 4, "fps": 1}[cfg["kind"]]
 
 
 def run_ours(args, cfg):
@@ -307,13 +310,29 @@ def run_ours(args, cfg):
     e2e_value = pairs * jobs / (e2e["ms"] * 1e-3) / 1e9
     e2e_pipe = run_e2e_pipelined(args, cfg, step, host_inputs, dev, ws)
     e2e_pipe_value = pairs * jobs / (e2e_pipe["ms"] * 1e-3) / 1e9
-    e2e_graph = None
+    e2e_graph = e2e_gp = None
     if not sharded:  # the sharded step runs NCCL collectives: not captured
         try:
             e2e_graph = run_e2e_pipelined(args, cfg, step, host_inputs, dev, ws, graphs=True)
         except Exception as e:  # capture unsupported -> reported as absent
             print(f"[bench] e2e graph capture failed ({e})", file=sys.stderr)
+        try:
+            e2e_gp = run_e2e_graph_pipeline(args, cfg, step, host_inputs, dev, ws)
+        except Exception as e:  # capture unsupported -> reported as absent
+            print(f"[bench] e2e graph capture failed ({e})", file=sys.stderr)
     e2e_graph_value = pairs * jobs / (e2e_graph["ms"] * 1e-3) / 1e9 if e2e_graph else None
+    if e2e_gp:
+        e2e_gp["value"] = pairs * jobs / (e2e_gp["ms"] * 1e-3) / 1e9
+    # context: the same pipelined step also reading every gradient back to the host
+    e2e_grads = None
+    if cfg["kind"] != "fps":
+        try:
+            e2e_grads = (run_e2e_graph_pipeline(args, cfg, step, host_inputs, dev, ws, grads=True)
+                         if not sharded else
+                         run_e2e_pipelined(args, cfg, step, host_inputs, dev, ws, grads=True))
+            e2e_grads["value"] = pairs * jobs / (e2e_grads["ms"] * 1e-3) / 1e9
+        except Exception as e:
+            print(f"[bench] e2e with gradient read-back failed ({e})", file=sys.stderr)
 
     # ---- the dominant kernel alone, for the roofline ----
     rows = None
@@ -326,23 +345,65 @@ def run_ours(args, cfg):
                 sharded=sharded,
                 clocks=clk.summary(), e2e=e2e, e2e_value=e2e_value, e2e_pipe=e2e_pipe,
                 e2e_pipe_value=e2e_pipe_value, e2e_graph=e2e_graph, e2e_graph_value=e2e_graph_value,
+                e2e_grads=e2e_grads, e2e_gp=e2e_gp,
                 roofline=roof)
 
 
-def run_e2e(args, cfg, step, host_inputs, dev, flush, ws):
-    pinned = [t.pin_memory() for t in host_inputs]
-    hi_bytes = sum(t.numel() * t.element_size() for t in pinned)
+class PackedInputs:
+    """A step's inputs packed into ONE pinned host byte buffer (each tensor at a
+    256-byte aligned offset), so a step's host->device transfer is one copy.
+    `views(dev_buf)` returns the tensors as views of a device copy of it, float
+    tensors as fresh autograd leaves (detach() shares the storage)."""
+
+    def __init__(self, host_inputs):
+        self.layout = []
+        off = 0
+        for t in host_inputs:
+            nb = t.numel() * t.element_size()
+            self.layout.append((off, nb, t.dtype, tuple(t.shape)))
+            off = (off + nb + 255) // 256 * 256
+        self.nbytes = off
+        self.host = torch.empty(off, dtype=torch.uint8, pin_memory=True)
+        for (o, nb, _, _), t in zip(self.layout, host_inputs):
+            self.host[o:o + nb].copy_(t.contiguous().view(-1).view(torch.uint8))
+        # bytes the step needs (padding excluded)
+        self.payload = sum(nb for _, nb, _, _ in self.layout)
+
+    def device_buffer(self, dev):
+        return torch.empty(self.nbytes, dtype=torch.uint8, device=dev)
+
+    def views(self, buf, grad):
+        out = []
+        for o, nb, dt, shape in self.layout:
+            t = buf[o:o + nb].view(dt).view(shape)
+            out.append(t.detach().requires_grad_() if grad and t.is_floating_point() else t)
+        return out
+
+
+def step_result(cfg, outs, grads):
+    """What a step reads back to the host: the loss (chamfer, knn) -- the
+    gradients stay on the device, where a training step consumes them -- or the
+    sampled indices (fps).  grads=True also reads back the gradients."""
+    outs = [o.detach() for o in outs]
+    return outs if grads else outs[:1]
+
+
+def run_e2e(args, cfg, step, host_inputs, dev, flush, ws, grads=False):
+    """Serial e2e: per step one H2D copy of the packed pinned inputs, the public
+    API forward + backward, and the D2H read of the step's result, back to back,
+    L2 flushed before each step."""
+    pk = PackedInputs(host_inputs)
+    dbuf = pk.device_buffer(dev)
     outs_host = None
+    use_grad = cfg["kind"] != "fps"
 
     def once():
         nonlocal outs_host
-        xs = [t.to(dev, non_blocking=True) for t in pinned]
-        if cfg["kind"] != "fps":
-            xs = [t.requires_grad_() if t.is_floating_point() else t for t in xs]
-        outs = [o.detach() for o in step(*xs)]
+        dbuf.copy_(pk.host, non_blocking=True)
+        res = step_result(cfg, step(*pk.views(dbuf, use_grad)), grads)
         if outs_host is None:
-            outs_host = [torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in outs]
-        for h, o in zip(outs_host, outs):
+            outs_host = [torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in res]
+        for h, o in zip(outs_host, res):
             h.copy_(o, non_blocking=True)
     for _ in range(max(3, args.warmup)):
         once()
@@ -363,38 +424,38 @@ def run_e2e(args, cfg, step, host_inputs, dev, flush, ws):
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         tot = float(t.item())
     bo = sum(h.numel() * h.element_size() for h in outs_host)
-    return {"ms": tot / args.steps, "h2d": hi_bytes, "d2h": bo}
+    return {"ms": tot / args.steps, "h2d": pk.payload, "d2h": bo}
 
 
-def run_e2e_pipelined(args, cfg, step, host_inputs, dev, ws, graphs=False):
+def run_e2e_pipelined(args, cfg, step, host_inputs, dev, ws, graphs=False, grads=False, nb=3):
     """The same public-API step and the same per-step copies as run_e2e, issued
     the way a training input pipeline runs them: step i's host->device input copy
-    (pinned, its own stream) overlaps step i-1's compute, and step i's
-    device->host result copy (third stream, from a device staging buffer the
-    compute stream fills) overlaps step i+1's compute.  Two device input
-    buffers, two staging buffers and two pinned output buffers rotate; every
-    step still copies all of its inputs in and all of its results out inside
-    the timed region, which spans K steps end to end (max over ranks).  With
-    graphs=True the compute stage of each buffer set (API step + staging copy)
-    is a captured CUDA graph, so the host issues only copies and replays."""
-    pinned = [t.pin_memory() for t in host_inputs]
+    (pinned, its own stream) overlaps the compute of earlier steps, and step i's
+    device->host result read (third stream) overlaps later steps' compute.  `nb`
+    device input buffers and pinned result buffers rotate; every step still
+    copies all of its inputs in and its result out inside the timed region, which
+    spans K steps end to end (max over ranks).  With graphs=True the compute
+    stage of each buffer set (the API step) is a captured CUDA graph, so the host
+    issues only copies and replays."""
+    pk = PackedInputs(host_inputs)
     s_in, s_cmp, s_out = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
-    nb = 2
-    dbuf = [[torch.empty(t.shape, dtype=t.dtype, device=dev) for t in pinned] for _ in range(nb)]
-    xsb = [[d.requires_grad_() if d.is_floating_point() and cfg["kind"] != "fps" else d for d in db]
-           for db in dbuf]
-    dout = [None] * nb  # results staged on the compute stream, read by the D2H stream
-    hout = [None] * nb
+    dbuf = [pk.device_buffer(dev) for _ in range(nb)]
+    use_grad = cfg["kind"] != "fps"
+    xsb = [pk.views(d, use_grad) for d in dbuf]
+    dout = [None] * nb  # each buffer set's result tensors (static under graphs)
     ev_in = [torch.cuda.Event() for _ in range(nb)]
     ev_used = [torch.cuda.Event() for _ in range(nb)]
     ev_out = [torch.cuda.Event() for _ in range(nb)]
 
     def compute(b):
-        outs = [o.detach() for o in step(*xsb[b])]
-        if dout[b] is None:
-            dout[b] = [torch.empty(o.shape, dtype=o.dtype, device=dev) for o in outs]
-        for d, o in zip(dout[b], outs):
-            d.copy_(o)
+        res = step_result(cfg, step(*xsb[b]), grads)
+        if graphs:
+            dout[b] = res
+        else:  # eager: results staged so the next step's allocations cannot reuse them
+            if dout[b] is None:
+                dout[b] = [torch.empty(o.shape, dtype=o.dtype, device=dev) for o in res]
+            for d, o in zip(dout[b], res):
+                d.copy_(o)
 
     gr = [None] * nb
     with torch.cuda.stream(s_cmp):
@@ -417,9 +478,7 @@ def run_e2e_pipelined(args, cfg, step, host_inputs, dev, ws, graphs=False):
         with torch.cuda.stream(s_in):
             if i >= nb:
                 s_in.wait_event(ev_used[b])  # the compute that read dbuf[b] is done
-            with torch.no_grad():
-                for d, h in zip(dbuf[b], pinned):
-                    d.copy_(h, non_blocking=True)
+            dbuf[b].copy_(pk.host, non_blocking=True)
             ev_in[b].record(s_in)
         with torch.cuda.stream(s_cmp):
             s_cmp.wait_event(ev_in[b])
@@ -452,7 +511,72 @@ def run_e2e_pipelined(args, cfg, step, host_inputs, dev, ws, graphs=False):
         t = torch.tensor([tot], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         tot = float(t.item())
-    return {"ms": tot / args.steps}
+    bo = sum(h.numel() * h.element_size() for h in hout[0])
+    return {"ms": tot / args.steps, "h2d": pk.payload, "d2h": bo}
+
+
+def run_e2e_graph_pipeline(args, cfg, step, host_inputs, dev, ws, grads=False):
+    """Pipelined e2e issued as CUDA graphs: two buffer sets, two graphs that
+    alternate.  Graph b holds step i's API forward + backward on buffer set b,
+    the D2H read of its result after it, and -- on a forked stream, overlapping
+    that compute -- the H2D copy of step i+1's packed inputs into the other
+    buffer set.  The timed region (one stream, K replays) therefore contains
+    every step's H2D copy (the first one issued before the first replay), its
+    compute and its result read; the host issues one replay per step."""
+    pk = PackedInputs(host_inputs)
+    dbuf = [pk.device_buffer(dev) for _ in range(2)]
+    use_grad = cfg["kind"] != "fps"
+    xsb = [pk.views(d, use_grad) for d in dbuf]
+    s_in = torch.cuda.Stream()
+    main = torch.cuda.Stream()
+    hout = [None, None]
+
+    def body(b):
+        cur = torch.cuda.current_stream()
+        s_in.wait_stream(cur)
+        with torch.cuda.stream(s_in):
+            dbuf[1 - b].copy_(pk.host, non_blocking=True)
+        res = step_result(cfg, step(*xsb[b]), grads)
+        if hout[b] is None:
+            hout[b] = [torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in res]
+        for h, o in zip(hout[b], res):
+            h.copy_(o, non_blocking=True)
+        cur.wait_stream(s_in)
+
+    main.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(main):
+        dbuf[0].copy_(pk.host, non_blocking=True)
+        for _ in range(3):
+            body(0)
+            body(1)
+    torch.cuda.synchronize()
+    gr = []
+    for b in range(2):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            body(b)
+        gr.append(g)
+    with torch.cuda.stream(main):
+        for i in range(max(3, args.warmup)):
+            gr[i % 2].replay()
+    torch.cuda.synchronize()
+    if ws > 1:
+        torch.distributed.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(main):
+        start.record()
+        dbuf[0].copy_(pk.host, non_blocking=True)  # step 0's inputs
+        for i in range(args.steps):
+            gr[i % 2].replay()
+        end.record()
+    end.synchronize()
+    tot = start.elapsed_time(end)
+    if ws > 1:
+        t = torch.tensor([tot], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        tot = float(t.item())
+    bo = sum(h.numel() * h.element_size() for h in hout[0])
+    return {"ms": tot / args.steps, "h2d": pk.payload, "d2h": bo}
 
 
 def kernel_roofline(cfg, inputs, dev, clocks, reps=20, rows=None):
@@ -861,12 +985,22 @@ def e2e_line(cfg, r):
         modes["pipelined_graph"] = (r["e2e_graph_value"], r["e2e_graph"]["ms"],
                                     "as pipelined, with each buffer set's API step captured as a "
                                     "CUDA graph (copies issued per step on their own streams)")
+    if r.get("e2e_gp"):
+        modes["graph_pipeline"] = (r["e2e_gp"]["value"], r["e2e_gp"]["ms"],
+                                   "two alternating CUDA graphs: step i's API step + result D2H, with "
+                                   "step i+1's H2D on a forked stream overlapping it; one replay per step")
     best = max(modes, key=lambda k: modes[k][0])
     out = {"value": round(modes[best][0], 2), "unit": unit_of(cfg),
            "h2d_bytes_per_step": r["e2e"]["h2d"], "d2h_bytes_per_step": r["e2e"]["d2h"],
            "ms_per_step": round(modes[best][1], 4), "mode": best,
            "modes": {k: {"value": round(v[0], 2), "ms_per_step": round(v[1], 4), "how": v[2]}
                      for k, v in modes.items()}}
+    g = r.get("e2e_grads")
+    if g:
+        out["with_gradient_readback"] = {
+            "value": round(g["value"], 2), "ms_per_step": round(g["ms"], 4),
+            "d2h_bytes_per_step": g["d2h"],
+            "how": "best pipelined mode, also reading every gradient back to pinned host memory each step"}
     return out
 
 

@@ -41,10 +41,16 @@ static __device__ unsigned g_fwd_device_error = 0;
 #ifndef TPO_CF_MINB
 #define TPO_CF_MINB 1
 #endif
+#ifndef TPO_CF_SUNROLL
+#define TPO_CF_SUNROLL 2
+#endif
+constexpr int CF_SUNROLL = TPO_CF_SUNROLL;
 constexpr int CF_R = TPO_CF_R;        // rows per lane
 constexpr int CF_RP = CF_R / 2;       // packed row pairs per lane
 constexpr int CF_C = 4;               // columns per sub-step
-constexpr int CF_CHUNK = 2 * CF_C;    // row-side chunk (columns per key)
+constexpr int CF_CHUNK = 2 * CF_C;    // fp32 row-side chunk (columns per key)
+constexpr int CF_HS = CF_CHUNK / CF_C;  // sub-steps per chunk
+constexpr int CH_CHUNK = 2 * CF_C;      // fp16 row-side chunk
 constexpr int CF_TILE_STEPS = 64;     // steps per shared-memory tile
 constexpr int CF_TILE = CF_TILE_STEPS * CF_C;
 #ifndef TPO_CF_MAXW
@@ -152,8 +158,8 @@ __global__ void __launch_bounds__(CF_MAXW * 32, TPO_CF_MINB)
     mbar_wait(&s_bar, phase, &g_fwd_device_error);
     phase ^= 1u;
     __syncthreads();
-    // duplicated {c,c} layout, NaN-padded to whole 8-column chunks
-    const int nsteps = ((ncols + CF_CHUNK - 1) / CF_CHUNK) * 2;
+    // duplicated {c,c} layout, NaN-padded to whole chunks
+    const int nsteps = ((ncols + CF_CHUNK - 1) / CF_CHUNK) * CF_HS;
     float2* dst = &s_col[0][0][0];
     for (int e = threadIdx.x; e < nsteps * CF_C * 3; e += blockDim.x) {
       const int col = e / 3;
@@ -184,18 +190,31 @@ __global__ void __launch_bounds__(CF_MAXW * 32, TPO_CF_MINB)
 
   for (int64_t tc = c0; tc < c1; tc += CF_TILE) {
     const int ncols = (int)min64(CF_TILE, c1 - tc);
-    const int nsteps = ((ncols + CF_CHUNK - 1) / CF_CHUNK) * 2;  // even: 8-column chunks
+    const int nsteps = ((ncols + CF_CHUNK - 1) / CF_CHUNK) * CF_HS;  // whole chunks
     if (tc != c0) {  // the first tile was staged together with the rows
       __syncthreads();
       stage(false, tc);
     }
     if (warp_active) {
+      // Column side, software-pipelined: a sub-step folds its columns' minima
+      // over the lane's rows (pend) and the warp-wide reduction of those is
+      // issued during the next sub-step, off the dependency chain.
+      unsigned pend[CF_C];
+      int pend_slot = -1;
       // Two 4-column sub-steps per iteration; the row-side chunk is 8 columns.
-#pragma unroll 1
-      for (int s = 0; s < nsteps; s += 2) {
+#pragma unroll CF_SUNROLL
+      for (int s = 0; s < nsteps; s += CF_HS) {
         float rm[CF_R];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
+        for (int h = 0; h < CF_HS; ++h) {
+          if (pend_slot >= 0) {
+#pragma unroll
+            for (int c = 0; c < CF_C; ++c) {
+              const unsigned w = redux_min_u32(pend[c]);
+              const unsigned bal = __ballot_sync(0xffffffffu, pend[c] == w);
+              if (lane == 0) s_wb[warp][pend_slot + c] = make_uint2(bal, w);
+            }
+          }
           const ulonglong2* cp = reinterpret_cast<const ulonglong2*>(&s_col[s + h][0][0]);
           const ulonglong2 xa = cp[0], xb = cp[1], ya = cp[2], yb = cp[3], za = cp[4], zb = cp[5];
           const u64 X[CF_C] = {xa.x, xa.y, xb.x, xb.y};
@@ -215,22 +234,27 @@ __global__ void __launch_bounds__(CF_MAXW * 32, TPO_CF_MINB)
             const float m = min3f(h == 0 ? best[r] : rm[r], d[0][r], d[1][r]);
             rm[r] = min3f(m, d[2][r], d[3][r]);
           }
-          // column side: warp min of the lanes' partial minima (bit pattern of a
-          // non-negative float orders like its value; NaN padding sorts last) and
-          // the ballot of lanes holding it -- the winning lane is resolved later
+          // column side: the lane's minimum over its rows per column; next
+          // sub-step, the warp min of those (bit pattern of a non-negative float
+          // orders like its value; NaN padding sorts last) and the ballot of
+          // lanes holding it -- the winning lane's row is resolved at the merge
 #pragma unroll
-          for (int c = 0; c < CF_C; ++c) {
-            const unsigned u = __float_as_uint(col_min<CF_R>(d[c]));
-            const unsigned w = redux_min_u32(u);
-            const unsigned bal = __ballot_sync(0xffffffffu, u == w);
-            if (lane == 0) s_wb[warp][(s + h) * CF_C + c] = make_uint2(bal, w);
-          }
+          for (int c = 0; c < CF_C; ++c) pend[c] = __float_as_uint(col_min<CF_R>(d[c]));
+          pend_slot = (s + h) * CF_C;
         }
         const int colbase = (int)(tc + s * CF_C);
 #pragma unroll
         for (int r = 0; r < CF_R; ++r) {
           if (rm[r] < best[r]) bchunk[r] = colbase;
           best[r] = rm[r];
+        }
+      }
+      if (pend_slot >= 0) {  // the last sub-step's columns
+#pragma unroll
+        for (int c = 0; c < CF_C; ++c) {
+          const unsigned w = redux_min_u32(pend[c]);
+          const unsigned bal = __ballot_sync(0xffffffffu, pend[c] == w);
+          if (lane == 0) s_wb[warp][pend_slot + c] = make_uint2(bal, w);
         }
       }
     }
@@ -341,7 +365,7 @@ __global__ void __launch_bounds__(CF_MAXW * 32, TPO_CF_MINB)
     mbar_wait(&s_bar, phase, &g_fwd_device_error);
     phase ^= 1u;
     __syncthreads();
-    const int nsteps = ((ncols + CF_CHUNK - 1) / CF_CHUNK) * 2;
+    const int nsteps = ((ncols + CH_CHUNK - 1) / CH_CHUNK) * 2;
     h2* dst = &s_col[0][0][0];
     for (int e = threadIdx.x; e < nsteps * CF_C * 3; e += blockDim.x) {
       const int col = e / 3;
@@ -372,7 +396,7 @@ __global__ void __launch_bounds__(CF_MAXW * 32, TPO_CF_MINB)
 
   for (int64_t tc = c0; tc < c1; tc += CF_TILE) {
     const int ncols = (int)min64(CF_TILE, c1 - tc);
-    const int nsteps = ((ncols + CF_CHUNK - 1) / CF_CHUNK) * 2;
+    const int nsteps = ((ncols + CH_CHUNK - 1) / CH_CHUNK) * 2;
     if (tc != c0) {
       __syncthreads();
       stage(false, tc);
@@ -909,8 +933,8 @@ __global__ void chamfer_bwd_from_keys_kernel(const T* __restrict__ xyz1, const T
     const T* other = (row ? xyz2 : xyz1) + b * Q * 3;
     const T q[3] = {own[0], own[1], own[2]};
     const int64_t base = (unsigned)key;
-    const int32_t j = row ? find_in_chunk<T, MODE, CF_CHUNK, true>(q, other, base,
-                                                                   min64(Q, base + CF_CHUNK), key)
+    constexpr int CH = std::is_same<T, float>::value ? CF_CHUNK : CH_CHUNK;
+    const int32_t j = row ? find_in_chunk<T, MODE, CH, true>(q, other, base, min64(Q, base + CH), key)
                           : (int32_t)base;
     const T gg = row ? g1 : g2;
     T* ga = (row ? gx1 : gx2) + u * 3;
@@ -1073,7 +1097,7 @@ int chamfer_finalize(int dtype, int flags, const void* x1, const void* x2, int64
     case TPO_F32:
       return exact ? TPO_FIN(float, TPO_ROUND_EXACT, CF_CHUNK, 1) : TPO_FIN(float, TPO_ROUND_FMA, CF_CHUNK, 1);
     case TPO_F16:
-      return TPO_FIN(__half, TPO_ROUND_EXACT, CF_CHUNK, 1);
+      return TPO_FIN(__half, TPO_ROUND_EXACT, CH_CHUNK, 1);
     case TPO_F64:
       return exact ? TPO_FIN(double, TPO_ROUND_EXACT, CG_C, CG_R) : TPO_FIN(double, TPO_ROUND_FMA, CG_C, CG_R);
   }
