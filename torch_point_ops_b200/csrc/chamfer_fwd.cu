@@ -745,7 +745,8 @@ __device__ __forceinline__ double to_d<__half>(__half v) { return (double)__half
 // scan costs one memory round trip instead of one per candidate.
 template <typename T, int MODE, int CH, bool Q_IS_ROW>
 __device__ __forceinline__ int32_t find_in_chunk(const T* q, const T* cloud, int64_t base,
-                                                 int64_t end, typename FinTraits<T>::K key) {
+                                                 int64_t end, typename FinTraits<T>::K key,
+                                                 T* xyz = nullptr) {
   T c[CH][3];
 #pragma unroll
   for (int k = 0; k < CH; ++k) {
@@ -759,6 +760,12 @@ __device__ __forceinline__ int32_t find_in_chunk(const T* q, const T* cloud, int
     const bool hit = Q_IS_ROW ? FinTraits<T>::template same<MODE>(q, c[k], key)
                               : FinTraits<T>::template same<MODE>(c[k], q, key);
     if (base + k < end && hit) found = k;
+  }
+  if (xyz) {  // the found point's coordinates, from the registers already loaded
+    found = found < 0 ? 0 : found;
+#pragma unroll
+    for (int k = 0; k < CH; ++k)
+      if (k == found) { xyz[0] = c[k][0]; xyz[1] = c[k][1]; xyz[2] = c[k][2]; }
   }
   return (int32_t)(base + (found < 0 ? 0 : found));
 }
@@ -926,20 +933,26 @@ __global__ void chamfer_bwd_from_keys_kernel(const T* __restrict__ xyz1, const T
     const bool row = t < n1;
     const int64_t u = row ? t : t - n1;
     const int64_t P = row ? N : M, Q = row ? M : N;
-    const int64_t b = u / P;
     const u64 key = row ? __ldg(keys1 + u) : __ldg(keys2 + u);
+    const int64_t b = total <= 0xffffffffll ? (int64_t)((unsigned)u / (unsigned)P) : u / P;
     if (Q == 0 || key == ~0ull) continue;
     const T* own = (row ? xyz1 : xyz2) + u * 3;
     const T* other = (row ? xyz2 : xyz1) + b * Q * 3;
     const T q[3] = {own[0], own[1], own[2]};
     const int64_t base = (unsigned)key;
     constexpr int CH = std::is_same<T, float>::value ? CF_CHUNK : CH_CHUNK;
-    const int32_t j = row ? find_in_chunk<T, MODE, CH, true>(q, other, base, min64(Q, base + CH), key)
-                          : (int32_t)base;
+    T pb[3];  // the neighbour's coordinates (rows: taken from the rescan's loads)
+    int32_t j;
+    if (row) {
+      j = find_in_chunk<T, MODE, CH, true>(q, other, base, min64(Q, base + CH), key, pb);
+    } else {
+      j = (int32_t)base;
+      const T* p = other + (int64_t)j * 3;
+      pb[0] = p[0]; pb[1] = p[1]; pb[2] = p[2];
+    }
     const T gg = row ? g1 : g2;
     T* ga = (row ? gx1 : gx2) + u * 3;
     T* gb = (row ? gx2 : gx1) + (b * Q + j) * 3;
-    const T* pb = other + (int64_t)j * 3;
     T v[3], nv[3];
 #pragma unroll
     for (int d = 0; d < 3; ++d) {
