@@ -26,7 +26,8 @@ graph-captured steps), each listed under e2e.modes, plus the pipelined number
 with every gradient also read back (e2e.with_gradient_readback).
 
 Other configs: 1, 3, 4 (knn), 5 / 5d (one 2^20-point cloud pair, row-sharded
-over the GPUs when N > 1), 2h (fp16), fps / fpsb (furthest point sampling).
+over the GPUs when N > 1), 5s / 5sd (the same scene at 2^17 points), 2h (fp16),
+fps / fpsb (furthest point sampling).
 """
 from __future__ import annotations
 
@@ -65,6 +66,12 @@ CONFIGS = {
               desc="Chamfer fwd+bwd B=1 N=M=2^20 fp32 LiDAR-like (config 5)"),
     "5d": dict(kind="chamfer", B=1, N=1 << 20, M=1 << 20, dtype="float64", gen="lidar",
                desc="Chamfer fwd+bwd B=1 N=M=2^20 fp64 LiDAR-like (config 5, fp64)"),
+    # config 5's LiDAR-like scene at 2^17 points: small cases of the config-5
+    # kernels for profiler captures and quick checks (not headline lines)
+    "5s": dict(kind="chamfer", B=1, N=1 << 17, M=1 << 17, dtype="float32", gen="lidar",
+               desc="Chamfer fwd+bwd B=1 N=M=2^17 fp32 LiDAR-like (config 5 scene, small)"),
+    "5sd": dict(kind="chamfer", B=1, N=1 << 17, M=1 << 17, dtype="float64", gen="lidar",
+                desc="Chamfer fwd+bwd B=1 N=M=2^17 fp64 LiDAR-like (config 5 scene, small, fp64)"),
     # furthest point sampling: the reference fps_benchmark.py's "100K points" case
     "fps": dict(kind="fps", B=1, N=100000, M=0, S=10000, dtype="float32", gen="normal",
                 desc="furthest_point_sampling B=1 P=100000 S=10000 fp32 N(0,1) (fps_benchmark.py)"),

@@ -514,6 +514,50 @@ __global__ void knn_bwd_kernel(const T* __restrict__ p1, const T* __restrict__ p
       }
       continue;
     }
+    if (D == 3) {
+      // Neighbours in batches of KB: all indices and grads of a batch are loaded
+      // first, then all their coordinates, so a query costs two dependent memory
+      // round trips per KB neighbours instead of two per neighbour.  The query's
+      // own gradient still sums the terms in k order; the neighbour's 3-vector
+      // goes out as one vector reduction plus one scalar.
+      constexpr int KB = 8;
+      T acc3[3] = {O::zero(), O::zero(), O::zero()};
+      if (i < L1) {
+        const T a[3] = {p1[t * 3], p1[t * 3 + 1], p1[t * 3 + 2]};
+        for (int k0 = 0; k0 < kk; k0 += KB) {
+          int64_t jj[KB];
+          T gg[KB];
+#pragma unroll
+          for (int u = 0; u < KB; ++u) {
+            const bool in = k0 + u < kk;
+            jj[u] = in ? idxs[t * K + k0 + u] : -1;
+            gg[u] = in ? gd[t * K + k0 + u] : O::zero();
+          }
+          T bb[KB][3];
+#pragma unroll
+          for (int u = 0; u < KB; ++u) {
+            const bool ok = jj[u] >= 0 && jj[u] < P2;
+            const T* q = p2 + (n * P2 + (ok ? jj[u] : 0)) * 3;
+#pragma unroll
+            for (int d = 0; d < 3; ++d) bb[u][d] = ok ? q[d] : O::zero();
+          }
+#pragma unroll
+          for (int u = 0; u < KB; ++u) {
+            if (jj[u] < 0 || jj[u] >= P2) continue;
+            T v[3];
+#pragma unroll
+            for (int d = 0; d < 3; ++d) {
+              v[d] = norm == 1 ? O::l1(gg[u], a[d], bb[u][d]) : O::l2(gg[u], a[d], bb[u][d]);
+              acc3[d] = O::add(acc3[d], v[d]);
+            }
+            O::atomic_sub3(g2 + (n * P2 + jj[u]) * 3, v);
+          }
+        }
+      }
+#pragma unroll
+      for (int d = 0; d < 3; ++d) g1[t * 3 + d] = acc3[d];
+      continue;
+    }
     T acc[KDMAX];
 #pragma unroll
     for (int d = 0; d < KDMAX; ++d) acc[d] = O::zero();
@@ -522,17 +566,6 @@ __global__ void knn_bwd_kernel(const T* __restrict__ p1, const T* __restrict__ p
         const int64_t j = idxs[t * K + k];
         if (j < 0 || j >= P2) continue;
         const T g = gd[t * K + k];
-        if (D == 3) {  // one vector reduction + one scalar for the neighbour's 3 components
-          T v[3];
-#pragma unroll
-          for (int d = 0; d < 3; ++d) {
-            const T a = p1[t * 3 + d], b = p2[(n * P2 + j) * 3 + d];
-            v[d] = norm == 1 ? O::l1(g, a, b) : O::l2(g, a, b);
-            acc[d] = O::add(acc[d], v[d]);
-          }
-          O::atomic_sub3(g2 + (n * P2 + j) * 3, v);
-          continue;
-        }
 #pragma unroll
         for (int d = 0; d < KDMAX; ++d) {
           if (d < D) {
@@ -555,8 +588,10 @@ int knn_backward(int dtype, const void* p1, const void* p2, const int64_t* l1, c
                  int64_t norm, const void* gd, void* g1, void* g2, cudaStream_t st) {
   const int64_t total = N * P1;
   if (total <= 0) return TPO_OK;
-  const int threads = 256;
-  const unsigned blocks = (unsigned)std::min<int64_t>((total + threads - 1) / threads, 148 * 16);
+  // one thread per query, a latency chain each: small blocks spread the
+  // queries evenly over the SMs
+  const int threads = 64;
+  const unsigned blocks = (unsigned)std::min<int64_t>((total + threads - 1) / threads, 148 * 64);
 #define TPO_KB(T)                                                                              \
   knn_bwd_kernel<T><<<blocks, threads, 0, st>>>((const T*)p1, (const T*)p2, l1, l2, idxs, N, P1, \
                                                 P2, (int)D, (int)K, (int)norm, (const T*)gd,    \
