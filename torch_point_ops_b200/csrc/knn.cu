@@ -188,7 +188,6 @@ __global__ void __launch_bounds__(KW * 32)
           // whether any query of this warp has a candidate at all
           V dv[KQ];
           unsigned bal[KQ];
-          unsigned any = 0;
           if constexpr (kPacked) {
             // two queries per packed fp32x2 sub/mul; the sums stay scalar .rn adds
             // (never fused), giving ((dx*dx + dy*dy) + dz*dz) exactly
@@ -207,12 +206,18 @@ __global__ void __launch_bounds__(KW * 32)
 #pragma unroll
             for (int i = 0; i < KQ; ++i) dv[i] = knn_dist<T, DT, NORM, MODE>(q[i], cc, Dn);
           }
+          // one vote for the whole step; the per-query ballots only when some
+          // lane holds a candidate
+          bool pr[KQ];
+          bool anyp = false;
 #pragma unroll
           for (int i = 0; i < KQ; ++i) {
-            bal[i] = __ballot_sync(0xffffffffu, qv[i] && cv && dv[i] < thr[i]);
-            any |= bal[i];
+            pr[i] = qv[i] && cv && dv[i] < thr[i];
+            anyp |= pr[i];
           }
-          if (any) {
+          if (__any_sync(0xffffffffu, anyp)) {
+#pragma unroll
+            for (int i = 0; i < KQ; ++i) bal[i] = __ballot_sync(0xffffffffu, pr[i]);
 #pragma unroll
             for (int i = 0; i < KQ; ++i) {
               while (bal[i]) {
