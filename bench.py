@@ -604,6 +604,8 @@ def kernel_roofline(cfg, inputs, dev, clocks, reps=20, rows=None):
 
     if cfg["kind"] == "fps":
         return fps_roofline(cfg, inputs, dev, clocks)
+    if cfg["kind"] == "knn":
+        return knn_roofline(cfg, inputs, dev, clocks)
     if cfg["kind"] != "chamfer" or cfg["dtype"] != "float32":
         return None
     ops = tpo._lib.chamfer_ops
@@ -638,6 +640,48 @@ def kernel_roofline(cfg, inputs, dev, clocks, reps=20, rows=None):
     if clocks.get("sm_mhz"):
         p2 = SMS * FP32_LANES * clocks["sm_mhz"] * 1e6 / INSTR_PER_PAIR / 1e9
         out["frac_at_measured_clock"] = round(achieved / p2, 4)
+    return out
+
+
+KNN_INSTR_PER_PAIR = 8  # (dx*dx + dy*dy) + dz*dz, every operation rounded: 3 sub, 3 mul, 2 add
+
+
+def knn_roofline(cfg, inputs, dev, clocks, reps=20):
+    """The knn forward kernel alone (the knn_forward op: one launch) against the
+    FP32 pipe: valid pairs (sum of lengths1 * lengths2) over its device time.
+    The knn distance is the reference's exactly rounded ((dx*dx + dy*dy) + dz*dz),
+    8 FP32-pipe operations per pair (no FMA), so the roofline is
+    148 SM x 128 lanes x clock / 8."""
+    import torch_point_ops_b200 as tpo
+
+    ops = tpo._lib.knn_ops
+    p1, p2, l1, l2 = [t.detach().contiguous() for t in inputs]
+    K = cfg["K"]
+    for _ in range(3):
+        ops.knn_forward(p1, p2, l1, l2, 2, K, -1)
+    flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)
+    tot = 0.0
+    for i in range(reps):
+        flush_l2(flush, i)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        ops.knn_forward(p1, p2, l1, l2, 2, K, -1)
+        b.record()
+        b.synchronize()
+        tot += a.elapsed_time(b)
+    ms = tot / reps
+    pairs = int((l1.long() * l2.long()).sum())
+    achieved = pairs / (ms * 1e-3) / 1e9
+    peak = SMS * FP32_LANES * MAX_SM_MHZ * 1e6 / KNN_INSTR_PER_PAIR / 1e9
+    out = {"bound": "fp32", "kernel": "knn_fwd_kernel", "achieved": round(achieved, 1),
+           "peak": round(peak, 1), "unit": "Gpair/s", "frac": round(achieved / peak, 4),
+           "peak_basis": "nominal FP32 pipe: 148 SM x 128 lanes x 1965 MHz / 8 instr per pair "
+                         "(MEASURED_PEAKS.json has no FP32 figure)",
+           "kernel_ms": round(ms, 4), "traffic": 1109248,
+           "traffic_basis": "dram__bytes_read.sum + dram__bytes_write.sum, profiles/knn_fwd_config4.md"}
+    if clocks.get("sm_mhz"):
+        p2_ = SMS * FP32_LANES * clocks["sm_mhz"] * 1e6 / KNN_INSTR_PER_PAIR / 1e9
+        out["frac_at_measured_clock"] = round(achieved / p2_, 4)
     return out
 
 
