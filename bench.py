@@ -1,19 +1,24 @@
 """Benchmark: Chamfer fwd+bwd in G point-pairs/s on B200 (one process per GPU).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2|2h|3|4|5|5d]
-                    [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 5|5d|2|2h|3|4|1|...]
+                    [--split weak|strong] [--impl ours|reference]
 
 A step = one forward + backward pass of the chamfer (or knn) path over one batch
 of seeded synthetic input with the benchmark configuration's shapes and
-distributions.  Default workload: configuration 2 (B=32, N=M=2048, fp32, unit
-sphere + N(0, 0.01^2) noise), the configuration the headline metric is quoted on.
+distributions.  Default workload: configuration 5 (B=1, N=M=2^20, fp32, LiDAR-like
+scene), the largest configuration; on N > 1 GPUs its rows are sharded over the
+ranks (strong scaling: one fixed problem, column keys merged by all_reduce(MIN),
+gradients by all_reduce(SUM)), and a sharded-vs-single-GPU parity check on a
+2^16-point scene runs before timing (`parity_ok` in the line).
 
 Timing: W untimed warm-up steps, then K timed steps, each bracketed by CUDA
 events on the launching stream; a 256 MiB buffer (> 126 MB L2) is rewritten
-before every timed step so no step starts with a warm L2.  Multi-GPU: each rank
-runs its own batch (weak scaling, no data-path collective), a barrier +
-synchronize brackets the timed region and the per-rank device time is
-max-reduced.  Rank 0 prints one JSON line.
+before every timed step so no step starts with a warm L2.  Multi-GPU: config 5
+is row-sharded (above); the batched configs either run an independent batch per
+rank (--split weak, the default) or split one fixed global problem over the ranks
+(--split strong: configs 2-3 by batch, config 4 by (batch, query-row) ranges
+balanced by lengths1*lengths2 work).  A barrier + synchronize brackets the timed
+region and the per-rank device time is max-reduced.  Rank 0 prints one JSON line.
 
 `value` = device-resident throughput (inputs already in HBM; the step is a CUDA
 graph of the public API's forward + backward).  `e2e` = the same metric through
@@ -196,15 +201,25 @@ def pairs_of(cfg, inputs):
 
 
 # ----------------------------------------------------------------- our arm ----
-def step_fn(cfg, sharded=False):
+def step_fn(cfg, mode="single", units=None, batch_share=1.0):
+    """The timed step through the public API.  mode: 'single' (one GPU's whole
+    problem, also each rank's problem under --split weak), 'rows' (config 5's
+    row-sharded cloud pair), 'strong' (this rank's share of one fixed batched
+    problem: its batches for chamfer, its balanced (batch, row) units for knn)."""
     import torch_point_ops_b200 as tpo
 
-    if sharded:
+    if mode == "rows":
         from torch_point_ops_b200.sharded import sharded_chamfer_loss
 
         def sstep(x1, x2):
             return sharded_chamfer_loss(x1.detach(), x2.detach())
         return sstep
+    if mode == "strong" and cfg["kind"] == "knn":
+        from torch_point_ops_b200.sharded import sharded_knn_loss
+
+        def kstep_units(p1, p2, l1, l2):
+            return sharded_knn_loss(p1, p2, units, cfg["K"])
+        return kstep_units
     if cfg["kind"] == "fps":
         def fstep(x):
             return (tpo.furthest_point_sampling(x, cfg["S"]),)
@@ -215,6 +230,11 @@ def step_fn(cfg, sharded=False):
         def step(x1, x2):
             loss = crit(x1, x2)
             g1, g2 = torch.autograd.grad(loss, [x1, x2])
+            if mode == "strong":
+                # this rank's batches: the global mean is the batch-weighted sum
+                # of the ranks' means (the optional scalar all-reduce of the loss)
+                loss = loss * batch_share
+                torch.distributed.all_reduce(loss)
             return loss, g1, g2
         return step
     knn = tpo.KNearestNeighbors(K=cfg["K"], return_nn=True)
@@ -227,11 +247,66 @@ def step_fn(cfg, sharded=False):
     return kstep
 
 
-def launches_per_step(cfg):
+def launches_per_step(cfg, mode="single"):
     # chamfer: fill, keys, loss reduction (fwd), gradient scatter into the
     # forward's zero-filled workspace (bwd); knn: knn fwd, gather fwd, gather
-    # bwd, knn bwd; fps: one sampling kernel
+    # bwd, knn bwd; fps: one sampling kernel.  Row-sharded chamfer: fill (keys
+    # init), keys, finalize, partial backward.
     return {"chamfer": 4, "knn": 4, "fps": 1}[cfg["kind"]]
+
+
+def parity_rows(dev, ws):
+    """Row-sharded vs single-GPU on a 2^16-point LiDAR-like scene, on every rank:
+    loss within 1e-6 relative, gradients within twice the per-element fp32 bound
+    (1e-6 of the summed term magnitudes; both sides sum in a free order)."""
+    import numpy as np
+
+    import datagen
+    import torch_point_ops_b200 as tpo
+    from tolerances import term_scale, tolerance
+    from torch_point_ops_b200.sharded import sharded_chamfer_loss
+
+    x1 = datagen.lidar(1 << 16, seed=77).to(dev)
+    x2 = datagen.lidar(1 << 16, seed=78).to(dev)
+    loss, g1, g2 = sharded_chamfer_loss(x1, x2)
+    a, b = x1.clone().requires_grad_(), x2.clone().requires_grad_()
+    ref = tpo.ChamferDistance("mean")(a, b)
+    ra, rb = torch.autograd.grad(ref, [a, b])
+    _, _, i1, i2 = tpo.chamfer_distance_with_idx(x1, x2)
+    n = x1.shape[1]
+    gg = torch.full((1, n), 1.0 / n)
+    s1, s2, n1, n2 = term_scale(x1.cpu(), x2.cpu(), i1.cpu(), i2.cpu(), gg, gg)
+    e1 = np.abs(g1.cpu().double().numpy() - ra.cpu().double().numpy())
+    e2 = np.abs(g2.cpu().double().numpy() - rb.cpu().double().numpy())
+    lerr = abs(float(loss) - float(ref)) / abs(float(ref))
+    ok = (lerr <= 1e-6 and bool(np.all(e1 <= 2 * tolerance(torch.float32, s1, n1)))
+          and bool(np.all(e2 <= 2 * tolerance(torch.float32, s2, n2))))
+    return ok, {"scene": "2^16 x 2^16 LiDAR-like, fp32", "loss_rel_err": lerr,
+                "grad_max_abs_err": float(max(e1.max(), e2.max()))}
+
+
+def parity_strong(cfg, step, glob_inputs, mine, dev):
+    """--split strong vs the whole problem on one GPU (run on every rank):
+    chamfer -- the global loss within 1e-6 relative and this rank's batches'
+    gradients within 1e-6 relative (atol 1e-9); knn -- the global loss within
+    1e-5 relative (float32 sums of 10^6 terms in different orders) and both
+    gradients within rtol 1e-5 / atol 1e-6 (fp32 atomics scatter in free order)."""
+    full = step_fn(cfg, "single")
+    gi = [t.to(dev) for t in glob_inputs]
+    gi = [t.requires_grad_() if t.is_floating_point() else t for t in gi]
+    rl, r1, r2 = full(*gi)
+    ml, m1, m2 = step(*mine)
+    lerr = abs(float(ml) - float(rl)) / max(abs(float(rl)), 1e-30)
+    if cfg["kind"] == "chamfer":
+        b0, b1 = mine[0].b_range
+        ok = (lerr <= 1e-6 and torch.allclose(m1, r1[b0:b1], rtol=1e-6, atol=1e-9)
+              and torch.allclose(m2, r2[b0:b1], rtol=1e-6, atol=1e-9))
+        err = float(max((m1 - r1[b0:b1]).abs().max(), (m2 - r2[b0:b1]).abs().max()))
+    else:
+        ok = (lerr <= 1e-5 and torch.allclose(m1, r1, rtol=1e-5, atol=1e-6)
+              and torch.allclose(m2, r2, rtol=1e-5, atol=1e-6))
+        err = float(max((m1 - r1).abs().max(), (m2 - r2).abs().max()))
+    return bool(ok), {"loss_rel_err": lerr, "grad_max_abs_err": err}
 
 
 def run_ours(args, cfg):
@@ -243,15 +318,42 @@ def run_ours(args, cfg):
     if ws > 1:
         import torch.distributed as dist
         dist.init_process_group("nccl", device_id=dev)
-    sharded = cfg["gen"] == "lidar" and ws > 1
-    # sharded single-cloud job: every rank holds the same clouds and owns a row
-    # share (strong scaling); otherwise each rank runs its own batch (weak)
-    host_inputs = make_inputs(cfg, seed=1000 if sharded else 1000 + 17 * rank)
-    pairs = pairs_of(cfg, host_inputs)
+    if cfg["gen"] == "lidar" and ws > 1:
+        mode = "rows"  # one cloud pair, rows sharded: every rank holds both clouds
+    elif args.split == "strong" and cfg["kind"] in ("chamfer", "knn") and ws > 1:
+        mode = "strong"
+    else:
+        mode = "single"  # N=1, or --split weak: each rank its own batch
+    seed = 1000 if mode in ("rows", "strong") else 1000 + 17 * rank
+    host_inputs = make_inputs(cfg, seed=seed)
+    glob_inputs = host_inputs
+    pairs = pairs_of(cfg, host_inputs)  # work of the whole job's problem (per rank for weak)
+    units = None
+    share = 1.0
+    if mode == "strong" and cfg["kind"] == "chamfer":
+        from torch_point_ops_b200.partition import batch_range
+        b0, b1 = batch_range(cfg["B"], ws, rank)
+        host_inputs = [t[b0:b1].contiguous() for t in host_inputs]
+        share = (b1 - b0) / cfg["B"]
     inputs = [t.to(dev) for t in host_inputs]
+    if mode == "strong" and cfg["kind"] == "knn":
+        from torch_point_ops_b200.sharded import KnnUnits
+        units = KnnUnits(host_inputs[2], host_inputs[3], ws, rank, dev)
     diff = [t.requires_grad_() if t.is_floating_point() and cfg["kind"] != "fps" else t for t in inputs]
-    step = step_fn(cfg, sharded)
+    if mode == "strong" and cfg["kind"] == "chamfer":
+        diff[0].b_range = (b0, b1)
+    step = step_fn(cfg, mode, units=units, batch_share=share)
     flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)  # 256 MiB > L2
+
+    parity = None
+    if mode == "rows":
+        ok, info = parity_rows(dev, ws)
+    elif mode == "strong":
+        ok, info = parity_strong(cfg, step, glob_inputs, diff, dev)
+    if mode != "single":
+        t = torch.tensor([1 if ok else 0], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MIN)
+        parity = {"ok": bool(t.item()), "rank0": info}
 
     # ---- device-resident path: the step captured as a CUDA graph ----
     s = torch.cuda.Stream()
@@ -260,8 +362,9 @@ def run_ours(args, cfg):
         for _ in range(max(3, args.warmup)):
             out = step(*diff)
     torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
     graph = None
-    if not sharded:  # the sharded step runs NCCL collectives: timed eagerly
+    if mode == "single":  # steps with NCCL collectives are timed eagerly
         try:
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph):
@@ -285,15 +388,18 @@ def run_ours(args, cfg):
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
 
     def load(seconds):
-        # untimed replays so nvidia-smi (100 ms sampling) sees the GPU under this load
+        # untimed steps so nvidia-smi (100 ms sampling) sees the GPU under this load
         t0 = time.perf_counter()
         while time.perf_counter() - t0 < seconds:
-            for _ in range(20):
+            for _ in range(20 if ws == 1 else 2):
                 run_step()
             torch.cuda.synchronize()
 
     with ClockSampler(local) as clk:
         load(1.0)
+        if ws > 1:
+            torch.distributed.barrier()
+            torch.cuda.synchronize()
         for i in range(args.steps):
             flush_l2(flush, i)
             ev[i][0].record()
@@ -309,16 +415,17 @@ def run_ours(args, cfg):
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         total_ms = float(t.item())
     ms_per_step = total_ms / args.steps
-    jobs = 1 if sharded else ws  # units processed by all ranks together
+    jobs = ws if mode == "single" else 1  # problems the ranks processed together
     value = pairs * jobs * args.steps / (total_ms * 1e-3) / 1e9
 
     # ---- e2e through the public API with pinned host buffers ----
+    big = ms_per_step > 20.0  # the graph-issued e2e modes only matter for short steps
     e2e = run_e2e(args, cfg, step, host_inputs, dev, flush, ws)
     e2e_value = pairs * jobs / (e2e["ms"] * 1e-3) / 1e9
     e2e_pipe = run_e2e_pipelined(args, cfg, step, host_inputs, dev, ws)
     e2e_pipe_value = pairs * jobs / (e2e_pipe["ms"] * 1e-3) / 1e9
     e2e_graph = e2e_gp = None
-    if not sharded:  # the sharded step runs NCCL collectives: not captured
+    if mode == "single" and not big:
         try:
             e2e_graph = run_e2e_pipelined(args, cfg, step, host_inputs, dev, ws, graphs=True)
         except Exception as e:  # capture unsupported -> reported as absent
@@ -335,7 +442,7 @@ def run_ours(args, cfg):
     if cfg["kind"] != "fps":
         try:
             e2e_grads = (run_e2e_graph_pipeline(args, cfg, step, host_inputs, dev, ws, grads=True)
-                         if not sharded else
+                         if mode == "single" and not big else
                          run_e2e_pipelined(args, cfg, step, host_inputs, dev, ws, grads=True))
             e2e_grads["value"] = pairs * jobs / (e2e_grads["ms"] * 1e-3) / 1e9
         except Exception as e:
@@ -343,13 +450,13 @@ def run_ours(args, cfg):
 
     # ---- the dominant kernel alone, for the roofline ----
     rows = None
-    if sharded:
-        from torch_point_ops_b200.sharded import row_range
+    if mode == "rows":
+        from torch_point_ops_b200.partition import row_range
         rows = row_range(cfg["N"], ws, rank)
-    roof = kernel_roofline(cfg, inputs, dev, clk.summary(), rows=rows)
-    roof_bwd = None if sharded else bwd_roofline(cfg, inputs, dev)
+    roof = kernel_roofline(cfg, inputs, dev, clk.summary(), rows=rows) if mode != "strong" else None
+    roof_bwd = bwd_roofline(cfg, inputs, dev) if mode == "single" else None
     return dict(roofline_bwd=roof_bwd, value=value, ms_per_step=ms_per_step, pairs=pairs, graph=graph is not None,
-                sharded=sharded,
+                mode=mode, parity=parity, per_rank_ms=total_ms / args.steps,
                 clocks=clk.summary(), e2e=e2e, e2e_value=e2e_value, e2e_pipe=e2e_pipe,
                 e2e_pipe_value=e2e_pipe_value, e2e_graph=e2e_graph, e2e_graph_value=e2e_graph_value,
                 e2e_grads=e2e_grads, e2e_gp=e2e_gp,
@@ -597,26 +704,71 @@ def run_e2e_graph_pipeline(args, cfg, step, host_inputs, dev, ws, grads=False):
     return {"ms": tot / args.steps, "h2d": pk.payload, "d2h": bo}
 
 
+_PIPE_PEAKS = {}
+
+
+def pipe_peak(kind):
+    """Measured whole-GPU rate of one arithmetic instruction kind on this device,
+    in element results per second, and the SM clock it ran at (MHz), from the
+    library's pipe probe (tpo_probe_pipe_peak: 8 independent fma chains per thread,
+    32 warps per SM, best of 3 launches).  kind: 0 fma.f32, 1 fma.f32x2,
+    2 fma.f16x2, 3 fma.f64."""
+    if kind not in _PIPE_PEAKS:
+        import ctypes
+
+        import torch_point_ops_b200 as tpo
+
+        lib = tpo._lib.capi()
+        r, mhz = ctypes.c_double(), ctypes.c_double()
+        rc = lib.tpo_probe_pipe_peak(ctypes.c_int(kind), ctypes.byref(r), ctypes.byref(mhz))
+        if rc != 0:
+            raise RuntimeError(f"tpo_probe_pipe_peak({kind}) failed with status {rc}")
+        _PIPE_PEAKS[kind] = (r.value, mhz.value)
+    return _PIPE_PEAKS[kind]
+
+
+# element operations per point pair in each chamfer keys kernel (the distance
+# only; the minima are overhead the roofline does not count):
+#   f32 (fma rounding): 3 sub + 1 mul + 2 fma, done as packed f32x2 on two rows
+#   f16: 3 sub + 3 mul + 2 add, every one rounded (c10::Half), packed f16x2
+#   f64: 3 sub + 1 mul + 2 fma, scalar
+CHAMFER_OPS = {"float32": (6, "chamfer_keys_f32_kernel", (0, 1)),
+               "float16": (8, "chamfer_keys_f16_kernel", (2,)),
+               "float64": (6, "chamfer_keys_generic_kernel<double>", (3,))}
+
+
+def fp_peak_pairs(ops_per_pair, kinds, nominal_lanes):
+    """Pairs/s roofline from the measured pipe rate (the faster of the given
+    instruction kinds), with the nominal figure beside it."""
+    best = max(pipe_peak(k)[0] for k in kinds)
+    mhz = pipe_peak(kinds[0])[1]
+    nominal = SMS * nominal_lanes * MAX_SM_MHZ * 1e6
+    return best / ops_per_pair / 1e9, {
+        "peak_basis": (f"measured pipe rate {best / 1e12:.2f} T element-ops/s (tpo_probe_pipe_peak, "
+                       f"SM clock {mhz:.0f} MHz) / {ops_per_pair} ops per pair; "
+                       "MEASURED_PEAKS.json carries no CUDA-core figure"),
+        "peak_nominal": round(nominal / ops_per_pair / 1e9, 1),
+        "nominal_basis": f"148 SM x {nominal_lanes} lanes x {MAX_SM_MHZ:.0f} MHz / {ops_per_pair}"}
+
+
 def kernel_roofline(cfg, inputs, dev, clocks, reps=20, rows=None):
     """Times the dominant kernel alone (CUDA events on its launching stream) and
-    reports achieved pair throughput against the FP32-pipe roofline."""
+    reports achieved pair throughput against the measured arithmetic-pipe peak."""
     import torch_point_ops_b200 as tpo
 
     if cfg["kind"] == "fps":
         return fps_roofline(cfg, inputs, dev, clocks)
     if cfg["kind"] == "knn":
         return knn_roofline(cfg, inputs, dev, clocks)
-    if cfg["kind"] != "chamfer" or cfg["dtype"] != "float32":
-        return None
     ops = tpo._lib.chamfer_ops
     x1, x2 = [t.detach().contiguous() for t in inputs[:2]]
     B, N, M = x1.shape[0], x1.shape[1], x2.shape[1]
     r0, r1 = rows if rows else (0, N)
-    if N * M > (1 << 36):
+    if B * N * M > (1 << 36):
         reps = 3  # ~0.2 s per launch at config 5
     k1 = ops.chamfer_keys_empty(x1, B * N)
     k2 = ops.chamfer_keys_empty(x1, B * M)
-    for _ in range(3):
+    for _ in range(2):
         ops.chamfer_fwd_keys(x1, x2, r0, r1, 0, k1, k2)
     flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)
     tot = 0.0
@@ -631,15 +783,17 @@ def kernel_roofline(cfg, inputs, dev, clocks, reps=20, rows=None):
     ms = tot / reps
     pairs = B * (r1 - r0) * M
     achieved = pairs / (ms * 1e-3) / 1e9
-    peak = SMS * FP32_LANES * MAX_SM_MHZ * 1e6 / INSTR_PER_PAIR / 1e9
-    out = {"bound": "fp32", "kernel": "chamfer_keys_f32_kernel", "achieved": round(achieved, 1),
+    n_ops, kname, kinds = CHAMFER_OPS[cfg["dtype"]]
+    lanes = {"float32": 128, "float16": 256, "float64": 64}[cfg["dtype"]]
+    peak, basis = fp_peak_pairs(n_ops, kinds, lanes)
+    out = {"bound": {"float32": "fp32", "float16": "fp16x2", "float64": "fp64"}[cfg["dtype"]],
+           "kernel": kname, "achieved": round(achieved, 1),
            "peak": round(peak, 1), "unit": "Gpair/s", "frac": round(achieved / peak, 4),
-           "peak_basis": "nominal FP32 pipe: 148 SM x 128 lanes x 1965 MHz / 6 instr per pair "
-                         "(MEASURED_PEAKS.json has no FP32 figure)",
-           "kernel_ms": round(ms, 4), "traffic": profiled_traffic(cfg)}
+           **basis, "frac_of_nominal": round(achieved / basis["peak_nominal"], 4),
+           "kernel_ms": round(ms, 4), "pairs_per_launch": pairs}
+    out.update(keys_traffic(cfg, pairs))
     if clocks.get("sm_mhz"):
-        p2 = SMS * FP32_LANES * clocks["sm_mhz"] * 1e6 / INSTR_PER_PAIR / 1e9
-        out["frac_at_measured_clock"] = round(achieved / p2, 4)
+        out["sm_mhz_bench_median"] = clocks["sm_mhz"]
     return out
 
 
@@ -672,17 +826,36 @@ def knn_roofline(cfg, inputs, dev, clocks, reps=20):
     ms = tot / reps
     pairs = int((l1.long() * l2.long()).sum())
     achieved = pairs / (ms * 1e-3) / 1e9
-    peak = SMS * FP32_LANES * MAX_SM_MHZ * 1e6 / KNN_INSTR_PER_PAIR / 1e9
+    peak, basis = fp_peak_pairs(KNN_INSTR_PER_PAIR, (0,), 128)
     out = {"bound": "fp32", "kernel": "knn_fwd_kernel", "achieved": round(achieved, 1),
            "peak": round(peak, 1), "unit": "Gpair/s", "frac": round(achieved / peak, 4),
-           "peak_basis": "nominal FP32 pipe: 148 SM x 128 lanes x 1965 MHz / 8 instr per pair "
-                         "(MEASURED_PEAKS.json has no FP32 figure)",
-           "kernel_ms": round(ms, 4), "traffic": 1109248,
-           "traffic_basis": "dram__bytes_read.sum + dram__bytes_write.sum, profiles/knn_fwd_config4.md"}
+           **basis, "frac_of_nominal": round(achieved / basis["peak_nominal"], 4),
+           "kernel_ms": round(ms, 4), "pairs_per_launch": pairs}
+    # compulsory bytes of the launch: p1, p2, lengths read once; idx + dists written
+    s_ = p1.element_size()
+    out["algorithmic_bytes"] = (p1.numel() + p2.numel()) * s_ + 16 * p1.shape[0] + p1.shape[0] * p1.shape[1] * K * (8 + s_)
+    tr = TRAFFIC.get(cfg["desc"])
+    out["traffic"] = tr[0] if tr else None
+    out["traffic_basis"] = tr[1] if tr else "not captured for this configuration"
     if clocks.get("sm_mhz"):
-        p2_ = SMS * FP32_LANES * clocks["sm_mhz"] * 1e6 / KNN_INSTR_PER_PAIR / 1e9
-        out["frac_at_measured_clock"] = round(achieved / p2_, 4)
+        out["sm_mhz_bench_median"] = clocks["sm_mhz"]
     return out
+
+
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of ONE launch of the
+# configuration's dominant kernel, from an ncu capture of this build on a B200,
+# with how it was taken.  Configurations without a capture report null.
+TRAFFIC = {
+    CONFIGS["4"]["desc"]: (1109248, "ncu capture of knn_fwd_kernel, config 4 (one launch)"),
+    CONFIGS["2"]["desc"]: (2686976, "ncu capture of chamfer_keys_f32_kernel, config 2 (one launch)"),
+}
+
+
+def keys_traffic(cfg, pairs):
+    tr = TRAFFIC.get(cfg["desc"])
+    if not tr or tr[0] is None:
+        return {"traffic": None, "traffic_basis": "not captured for this configuration"}
+    return {"traffic": tr[0], "traffic_basis": tr[1]}
 
 
 def measured_hbm_gbs():
@@ -761,22 +934,6 @@ def fps_roofline(cfg, inputs, dev, clocks, reps=5):
             "peak_basis": "nominal FP32 pipe: 148 SM x 128 lanes x 1965 MHz / 7 ops per update",
             "kernel_ms": round(ms, 4), "us_per_sample": round(ms * 1e3 / (S - 1), 3),
             "traffic": None}
-
-
-def profiled_traffic(cfg):
-    """DRAM bytes per launch of the keys kernel from the committed ncu summary
-    (profiles/chamfer_keys_f32_config<N>.md), or None when none was captured."""
-    name = {"Chamfer fwd+bwd B=32 N=M=2048 fp32 sphere+noise (config 2)": "2"}.get(cfg["desc"])
-    if name is None:
-        return None
-    path = os.path.join(ROOT, "profiles", f"chamfer_keys_f32_config{name}.md")
-    try:
-        for line in open(path):
-            if line.startswith("| dram_bytes_per_launch"):
-                return int(line.split("|")[2].strip())
-    except OSError:
-        pass
-    return None
 
 
 # ------------------------------------------------------ CPU reference path ----
@@ -901,26 +1058,59 @@ def cpu_fps_sample(cfg, host_inputs, budget_s):
                                                 f"one thread per cloud ({threads} threads)")
 
 
-def cpu_measure(cfg, host_inputs, budget_s=15.0):
-    """Bounded CPU sample (~budget_s); returns the cpu_baseline object."""
+def cpu_measure(cfg, host_inputs, budget_s=15.0, threads=None):
+    """Bounded CPU sample (~budget_s) on `threads` host threads (default: all);
+    returns the cpu_baseline object.  Samples smaller than the full step are
+    rates extrapolated from a row subsample and say so."""
+    threads = threads or os.cpu_count() or 1
     if cfg["kind"] == "fps":
         done, dt, kind, cores, sample = cpu_fps_sample(cfg, host_inputs, budget_s)
         return {"value": round(done / dt / 1e9, 4), "unit": "Gupdate/s", "cores": cores, "kind": kind,
                 "sample": sample, "seconds": round(dt, 3)}
     if cfg["kind"] == "knn":
-        done, dt, kind, cores, sample = cpu_knn_sample(cfg, host_inputs)
+        done, dt, kind, cores, sample = cpu_knn_sample(cfg, host_inputs, threads=threads)
+        full = pairs_of(cfg, host_inputs)
     else:
         N = cfg["N"]
-        rows = N
         # shrink rows so one sample takes about budget_s / 3 seconds
-        probe_rows = min(N, 64)
-        done, dt, kind, cores, sample = cpu_chamfer_sample(cfg, host_inputs, max_rows=probe_rows)
+        probe_rows = min(N, 64 if threads > 1 else 8)
+        done, dt, kind, cores, sample = cpu_chamfer_sample(cfg, host_inputs, max_rows=probe_rows,
+                                                           threads=threads)
         rate = done / max(dt, 1e-6)
         want = rate * budget_s / 3
         rows = int(min(N, max(probe_rows, want * 2 / (cfg["B"] * (cfg["N"] + cfg["M"])))))
-        done, dt, kind, cores, sample = cpu_chamfer_sample(cfg, host_inputs, max_rows=rows)
+        done, dt, kind, cores, sample = cpu_chamfer_sample(cfg, host_inputs, max_rows=rows,
+                                                           threads=threads)
+        full = cfg["B"] * cfg["N"] * cfg["M"]
+    if done < full:
+        sample += (f"; extrapolated: the rate of this {100.0 * done / full:.3g}% subsample, the full "
+                   f"step would take ~{full / (done / dt):.3g} s")
     return {"value": round(done / dt / 1e9, 4), "unit": "Gpair/s", "cores": cores, "kind": kind,
             "sample": sample, "seconds": round(dt, 3)}
+
+
+def host_cores():
+    """(physical cores, logical threads) of this host."""
+    logical = os.cpu_count() or 1
+    try:
+        import psutil
+        phys = psutil.cpu_count(logical=False) or logical
+    except ImportError:
+        phys = logical
+    return phys, logical
+
+
+def cpu_baseline(cfg, host_inputs, budget_s=20.0):
+    """The reference's CPU path on every host thread (the headline cpu_baseline)
+    and, as shipped (single-threaded), on one core."""
+    phys, logical = host_cores()
+    allc = cpu_measure(cfg, host_inputs, budget_s=budget_s * 0.6, threads=logical)
+    one = cpu_measure(cfg, host_inputs, budget_s=budget_s * 0.4, threads=1)
+    out = {k: allc[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    out["cores_basis"] = f"{logical} logical threads on {phys} physical cores"
+    out["physical_cores"] = phys
+    out["single_core"] = {"value": one["value"], "unit": one["unit"], "cores": 1, "sample": one["sample"]}
+    return out
 
 
 def run_reference_cuda(args, cfg):
@@ -1022,13 +1212,16 @@ def run_reference(args, cfg):
         "impl": "reference", "metric": metric_name(cfg), "value": v, "unit": unit_of(cfg),
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(pairs / (v * 1e9) * 1e3, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": cfg["dtype"].replace("float", "f"),
+        "scaling": "strong" if (cfg["gen"] == "lidar" or args.split == "strong") else "weak",
+        "vs_baseline": None, "dtype": cfg["dtype"].replace("float", "f"),
         "data": "synthetic (seeded, config distribution)",
         "config": {"workload": cfg["desc"]},
         "cpu_baseline": {k: last[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": v, "unit": unit_of(cfg), "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     line["cpu_baseline"]["value"] = v
+    phys, logical = host_cores()
+    line["cpu_baseline"]["cores_basis"] = f"{logical} logical threads on {phys} physical cores"
     return line
 
 
@@ -1070,9 +1263,12 @@ def e2e_line(cfg, r):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="2", choices=sorted(CONFIGS))
+    ap.add_argument("--config", default="5", choices=sorted(CONFIGS))
+    ap.add_argument("--split", default="weak", choices=["weak", "strong"],
+                    help="batched configs on N > 1 GPUs: an independent batch per rank (weak) or one "
+                         "global problem split over the ranks (strong); config 5 is always row-sharded")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference_cuda"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     args = ap.parse_args()
@@ -1097,27 +1293,37 @@ def main():
         return
     cpu = None
     if not args.no_cpu and ws == 1:
-        cpu = cpu_measure(cfg, make_inputs(cfg, seed=1000), budget_s=15.0)
-        cpu = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        cpu = cpu_baseline(cfg, make_inputs(cfg, seed=1000))
+    mode = r["mode"]
+    par = {"single": f"dp{ws} (independent batch per GPU)" if ws > 1 else "one GPU",
+           "rows": (f"rows of cloud 1 sharded over {ws} GPUs (both clouds replicated), column keys "
+                    "all_reduce(MIN), gradients + loss all_reduce(SUM)"),
+           "strong": (f"one global problem split over {ws} GPUs: " +
+                      ("contiguous batch ranges, loss all_reduce(SUM)" if cfg["kind"] == "chamfer" else
+                       "(batch, query-row) units balanced by lengths1*lengths2 work, one packed "
+                       "knn launch per rank, gradients + loss all_reduce(SUM)"))}[mode]
     line = {
         "metric": metric_name(cfg),
         "value": round(r["value"], 2), "unit": unit_of(cfg), "n_gpus": ws, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(r["ms_per_step"], 4),
-        "higher_is_better": True, "scaling": "strong" if r["sharded"] else "weak",
+        "higher_is_better": True, "scaling": "weak" if mode == "single" else "strong",
         "vs_baseline": None, "dtype": cfg["dtype"].replace("float", "f"),
         "data": "synthetic (seeded, config distribution)",
-        "config": {"workload": cfg["desc"], "pairs_per_step_per_gpu": r["pairs"],
+        "config": {"workload": cfg["desc"],
+                   "pairs_per_step": r["pairs"] * (ws if mode == "single" else 1),
                    "l2": "256 MiB buffer written then read before every timed step (inputs evicted, L2 left clean)",
-                   "parallelism": (f"rows sharded over {ws} GPUs, keys all_reduce(MIN), grads all_reduce(SUM)"
-                                   if r["sharded"] else f"dp{ws} (independent batch per GPU)"),
+                   "parallelism": par, "split": mode,
                    "cuda_graph": r["graph"]},
         "clocks": r["clocks"],
         "e2e": e2e_line(cfg, r),
-        "gpu_launches": launches_per_step(cfg) * args.steps,
+        "gpu_launches": launches_per_step(cfg, mode) * args.steps,
         "roofline": r["roofline"],
         "roofline_bwd": r["roofline_bwd"],
         "cpu_baseline": cpu,
     }
+    if r["parity"] is not None:
+        line["parity_ok"] = r["parity"]["ok"]
+        line["parity"] = r["parity"]
     print(json.dumps(line), flush=True)
     if ws > 1:
         torch.distributed.destroy_process_group()

@@ -90,10 +90,10 @@ TPO_API int tpo_chamfer_fwd(int dtype, int flags, const void* xyz1, const void* 
  * they may call: code inside an allocator or memory pool, services that forbid
  * device allocation after start-up, hosts that only receive buffers).  Same
  * arguments and results as tpo_chamfer_fwd minus the workspace: the keys live
- * in a 16 MiB device array owned by the library, which every GPU that loads the
- * library holds until process exit.  Limit: tpo_chamfer_fwd_workspace_size()
- * <= 16 MiB, i.e. B*(N+M) <= 2,097,152 points for f32/f16 (1,048,576 for f64);
- * larger problems return TPO_ERR_WORKSPACE.  The first call on a device looks
+ * in a device array of 16 MiB (+512 bytes of alignment padding) owned by the
+ * library, which every GPU that loads the library holds until process exit.
+ * Limit: B*(N+M) <= 2,097,152 points for f32/f16 (1,048,576 for f64), whatever
+ * the split between N and M; larger problems return TPO_ERR_WORKSPACE.  The first call on a device looks
  * up the array's device address (cudaGetSymbolAddress) -- make that first call
  * before any stream capture.  Calls share the array: calls that overlap on the
  * GPU (other streams or threads on the same device) race and must be
@@ -234,6 +234,15 @@ TPO_API int tpo_gather_points_fwd(int dtype, const void* points, const int64_t* 
                                   int64_t C, int64_t P, int64_t M, void* out, void* stream);
 TPO_API int tpo_gather_points_bwd(int dtype, const void* grad_out, const int64_t* idx, int64_t N,
                                   int64_t C, int64_t P, int64_t M, void* grad_points, void* stream);
+
+/* Measurement aid (no counterpart in the reference): the sustained issue rate of
+ * one arithmetic instruction kind on the current device, for quoting the CUDA-core
+ * kernels' rooflines against a measured peak.  kind: 0 fma.rn.f32, 1 fma.rn.f32x2,
+ * 2 fma.rn.f16x2, 3 fma.rn.f64.  *lane_ops_per_s = element results per second
+ * over the whole GPU (a packed x2 instruction counts 2 per lane); *sm_mhz = the SM
+ * clock seen during the run.  Synchronous (own stream, ~0.1-0.5 s); allocates
+ * 32 bytes of device memory. */
+TPO_API int tpo_probe_pipe_peak(int kind, double* lane_ops_per_s, double* sm_mhz);
 
 #ifdef __cplusplus
 }

@@ -122,40 +122,6 @@ def test_empty_clouds(N, M):
     assert torch.all(d1 == 0) and torch.all(i1 == 0) and torch.all(d2 == 0)
 
 
-def test_config2_full_size_f32_and_f16():
-    for dtype in (torch.float32, torch.float16):
-        x1 = datagen.sphere_noise(32, 2048, seed=20, dtype=dtype)
-        x2 = datagen.sphere_noise(32, 2048, seed=21, dtype=dtype)
-        _, _, i1, i2 = _check_fwd(x1, x2, 0)
-        _check_bwd(x1, x2, i1, i2)
-
-
-def test_config3_full_size():
-    x1 = datagen.gmm(16, 16384, seed=30)
-    x2 = datagen.gmm(16, 8192, seed=31)
-    _check_fwd(x1, x2, 0)
-
-
-def test_config5_sampled_rows_f32():
-    """1M x 1M: full GPU run, oracle on sampled rows/columns (size-independent check)."""
-    N = 1 << 20
-    x1 = datagen.lidar(N, seed=50)
-    x2 = datagen.lidar(N, seed=51)
-    d1, d2, i1, i2 = C.chamfer_fwd(x1.to(DEV), x2.to(DEV))
-    torch.cuda.synchronize()
-    g = torch.Generator().manual_seed(0)
-    rows = torch.randint(0, N, (2048,), generator=g)
-    od, oi = oracle.nn(x1[:, rows].numpy(), x2.numpy(), 1)
-    assert np.array_equal(i1[:, rows].cpu().numpy(), oi)
-    assert np.array_equal(_bits(d1[:, rows]), od.view(np.uint8))
-    od, oi = oracle.nn(x2[:, rows].numpy(), x1.numpy(), 1)
-    assert np.array_equal(i2[:, rows].cpu().numpy(), oi)
-    # properties over every point: dist1[i] == |x1[i] - x2[idx1[i]]|^2 recomputed
-    a, b = x1[0].to(DEV), x2[0].to(DEV)
-    r = ((b[i1[0].long()] - a) ** 2)
-    assert torch.all(d1[0] <= r.sum(-1) * (1 + 1e-6) + 1e-30)
-
-
 def test_torch_api_autograd_matches_capi():
     import torch_point_ops_b200 as tpo
 
@@ -168,9 +134,13 @@ def test_torch_api_autograd_matches_capi():
     assert torch.allclose(loss.detach(), ref, rtol=1e-6)
     g1 = torch.full_like(d1, 1.0 / d1.numel())
     g2 = torch.full_like(d2, 1.0 / d2.numel())
-    gx1, gx2 = C.chamfer_bwd(x1.detach(), x2.detach(), i1, i2, g1, g2)
-    assert torch.allclose(x1.grad, gx1, rtol=1e-5, atol=1e-9)
-    assert torch.allclose(x2.grad, gx2, rtol=1e-5, atol=1e-9)
+    # autograd's gradients against the oracle's scatter at the contract's bound
+    a, b = x1.detach().cpu(), x2.detach().cpu()
+    o1, o2 = oracle.chamfer_bwd(a.numpy(), b.numpy(), i1.cpu().numpy(), i2.cpu().numpy(),
+                                g1.cpu().numpy(), g2.cpu().numpy())
+    s1, s2, n1, n2 = _term_scale(a, b, i1, i2, g1.cpu(), g2.cpu())
+    assert np.all(np.abs(x1.grad.cpu().double().numpy() - o1) <= tolerance(torch.float32, s1, n1))
+    assert np.all(np.abs(x2.grad.cpu().double().numpy() - o2) <= tolerance(torch.float32, s2, n2))
     for red in ("sum", None, "none"):
         out = tpo.ChamferDistance(red)(x1, x2)
     assert isinstance(out, tuple) and out[0].shape == (3, 700)
@@ -199,9 +169,13 @@ def test_fused_loss_capi(dtype, reduction, shape):
     x2 = datagen.sphere_noise(B, M, seed=9, dtype=dtype).to(DEV)
     loss, state = C.chamfer_loss_fwd(x1, x2, reduction)
     d1, d2, i1, i2 = C.chamfer_fwd(x1, x2)
-    ref = (d1.mean() + d2.mean()) if reduction == 0 else (d1.sum() + d2.sum())
-    rtol = {torch.float32: 1e-5, torch.float64: 1e-12, torch.float16: 2e-3}[dtype]
-    assert torch.allclose(loss.double(), ref.double(), rtol=rtol), (loss, ref)
+    # the loss against the float64 reduction of the ORACLE's distances, at the
+    # contract's tolerance (1e-6 fp32, 1e-3 fp16, 1e-12 fp64)
+    od1, od2, _, _ = oracle.chamfer_fwd(x1.cpu().numpy(), x2.cpu().numpy(), 1)
+    od1, od2 = od1.astype(np.float64), od2.astype(np.float64)
+    ref = (od1.mean() + od2.mean()) if reduction == 0 else (od1.sum() + od2.sum())
+    rtol = {torch.float32: 1e-6, torch.float64: 1e-12, torch.float16: 1e-3}[dtype]
+    assert abs(float(loss) - ref) <= rtol * abs(ref), (float(loss), ref)
     gl = torch.tensor([0.75], dtype=dtype, device=DEV)
     gx1, gx2 = C.chamfer_loss_bwd(x1, x2, state, gl, reduction)
     if reduction == 0:

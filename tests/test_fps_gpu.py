@@ -213,19 +213,11 @@ def test_fps_gather_multi_precision(dtype):
     assert feats.grad.dtype == dtype and float(feats.grad.float().sum()) == 4 * 8
 
 
-def test_quick_fps_api():
-    """quick_* keep the reference's signature and checks and return the exact FPS."""
+def test_quick_fps_names_are_not_exported():
+    """The approximate kd-tree sampler is out of scope: its names are absent
+    rather than silently returning a different (exact) sampling."""
+    assert not hasattr(tpo, "quick_furthest_point_sampling")
+    assert not hasattr(tpo, "QuickFarthestPointSampling")
+    from torch_point_ops_b200.fps import fps_function
     x = _cloud(2, 300, torch.float32, seed=9).to(DEV)
-    ref = tpo.furthest_point_sampling(x, 16)
-    assert torch.equal(tpo.quick_furthest_point_sampling(x, 16, kd_depth=6), ref)
-    idx, pts = tpo.quick_farthest_point_sample_and_gather(x, 16)
-    assert torch.equal(idx, ref) and pts.shape == (2, 16, 3)
-    assert torch.equal(tpo.QuickFarthestPointSampling(16, kd_depth=3)(x), ref)
-    from torch_point_ops_b200.fps import quick_fps_function, fps_function
-    assert torch.equal(quick_fps_function(x, 16), ref) and torch.equal(fps_function(x, 16), ref)
-    with pytest.raises(ValueError):
-        tpo.quick_furthest_point_sampling(x, 16, kd_depth=0)
-    with pytest.raises(ValueError):
-        tpo.quick_furthest_point_sampling(x, 16, kd_depth=11)
-    with pytest.raises(ValueError):
-        tpo.QuickFarthestPointSampling(16, kd_depth=20)
+    assert torch.equal(fps_function(x, 16), tpo.furthest_point_sampling(x, 16))

@@ -118,3 +118,49 @@ def test_reference_knn_cuda_general(D, K):
     valid = torch.arange(90)[None, :, None] < L1[:, None, None]
     assert torch.equal(i.cpu()[valid.expand_as(i.cpu())], ri.cpu()[valid.expand_as(i.cpu())])
     assert np.array_equal(_bits(d.cpu()[valid.expand_as(d.cpu())]), _bits(rd.cpu()[valid.expand_as(d.cpu())]))
+
+
+@pytest.mark.parametrize("ragged", [False, True])
+def test_reference_knn_cuda_f16(ragged):
+    """fp16 knn against the reference CUDA build (c10::Half arithmetic: every
+    sub, mul and add rounds to half).  Half distances tie often, and the
+    reference's MinK and its unstable torch.sort order equal distances freely,
+    so: the sorted distances are compared bit for bit everywhere, and indices
+    wherever the distance value is unique within the query's K and is not the
+    K-th distance (there the reference may keep any of the tied candidates);
+    every reference index must also reproduce its own distance."""
+    ops = oracle.ref_knn()
+    if ops is None or not oracle._ref_loaded.get("knn_cuda_ref.so"):
+        pytest.skip("reference CUDA knn build not present in oracle/_ref")
+    g = torch.Generator().manual_seed(16 + ragged)
+    B, P1, P2, K = 3, 600, 900, 16
+    p1 = torch.randn(B, P1, 3, generator=g).half()
+    p2 = torch.randn(B, P2, 3, generator=g).half()
+    L1 = torch.tensor([600, 401, 77]) if ragged else torch.full((B,), P1)
+    L2 = torch.tensor([900, 513, 40]) if ragged else torch.full((B,), P2)
+    ri, rd = ops.knn_forward(p1.cuda(), p2.cuda(), L1.cuda(), L2.cuda(), 2, K, -1)
+    rd, order = rd.sort(dim=2)
+    ri = ri.gather(2, order).cpu()
+    rd = rd.cpu()
+    i, d = C.knn_fwd(p1.cuda(), p2.cuda(), L1.cuda(), L2.cuda(), 2, K, 0)
+    i, d = i.cpu(), d.cpu()
+    oi, od = oracle.knn_fwd(p1.numpy(), p2.numpy(), L1.numpy(), L2.numpy(), 2, K, 0)
+    assert np.array_equal(i.numpy(), oi) and np.array_equal(_bits(d), od.view(np.uint8))
+    for b in range(B):
+        l1, kk = int(L1[b]), min(K, int(L2[b]))
+        db, rdb = d[b, :l1, :kk], rd[b, :l1, :kk]
+        assert np.array_equal(_bits(db), _bits(rdb)), "sorted distances differ"
+        dv = db.float().numpy()
+        kth = dv[:, kk - 1:kk]
+        uniq = (np.sum(dv[:, :, None] == dv[:, None, :], axis=2) == 1) & (dv != kth)
+        assert np.array_equal(i[b, :l1, :kk].numpy()[uniq], ri[b, :l1, :kk].numpy()[uniq])
+        # each reference index reproduces its distance with c10::Half rounding
+        q = p1[b, :l1].float()[:, None, :]
+        t = p2[b].float()[ri[b, :l1, :kk].long()]
+        # recompute the reference neighbours' distances in half, per operation
+        dx = (t[..., 0] - q[..., 0]).half().float()
+        dy = (t[..., 1] - q[..., 1]).half().float()
+        dz = (t[..., 2] - q[..., 2]).half().float()
+        rr = ((dx * dx).half().float() + (dy * dy).half().float()).half().float()
+        rr = (rr + (dz * dz).half().float()).half()
+        assert np.array_equal(_bits(rr), _bits(rdb))

@@ -23,16 +23,30 @@ def _run(rank, world, port, x1, x2, q, dtype=torch.float32):
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
     a, b = x1.to(dev, dtype), x2.to(dev, dtype)
-    loss, g1, g2 = sharded_chamfer_loss(a, b)
+    loss, g1s, g2s = sharded_chamfer_loss(a, b)
     if rank == 0:
+        import numpy as np
+
+        import capi_util as C
+        from tolerances import term_scale, tolerance
+
         ra = a.clone().requires_grad_()
         rb = b.clone().requires_grad_()
         ref = tpo.ChamferDistance("mean")(ra, rb)
         ref.backward()
-        rt, at = (1e-5, 1e-10) if dtype == torch.float32 else (1e-12, 1e-17)
-        ok = (torch.allclose(loss, ref, rtol=rt) and
-              torch.allclose(g1, ra.grad, rtol=rt, atol=at) and
-              torch.allclose(g2, rb.grad, rtol=rt, atol=at))
+        rt = 1e-6 if dtype == torch.float32 else 1e-12
+        ok = abs(float(loss) - float(ref)) <= rt * abs(float(ref))
+        # gradients: both sides are sums in a free order, so each may sit the
+        # per-element bound away from the exact sum -> twice the bound apart
+        _, _, i1, i2 = C.chamfer_fwd(a, b)
+        B, N, M = a.shape[0], a.shape[1], b.shape[1]
+        g1 = torch.full((B, N), 1.0 / (B * N), dtype=dtype)
+        g2 = torch.full((B, M), 1.0 / (B * M), dtype=dtype)
+        s1, s2, n1, n2 = term_scale(a.cpu(), b.cpu(), i1, i2, g1, g2)
+        e1 = np.abs(g1s.cpu().double().numpy() - ra.grad.cpu().double().numpy())
+        e2 = np.abs(g2s.cpu().double().numpy() - rb.grad.cpu().double().numpy())
+        ok = ok and bool(np.all(e1 <= 2 * tolerance(dtype, s1, n1)))
+        ok = ok and bool(np.all(e2 <= 2 * tolerance(dtype, s2, n2)))
         q.put(bool(ok))
     dist.destroy_process_group()
 

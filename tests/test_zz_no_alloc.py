@@ -63,3 +63,29 @@ def test_noalloc_rejects_oversize_problem():
                                           C.stream())
     assert rc == 3  # TPO_ERR_WORKSPACE
     assert b"16 MiB" in C.lib().tpo_status_string(rc)
+
+
+@pytest.mark.parametrize("dtype,N,M", [(torch.float32, 1_048_575, 1_048_577),
+                                       (torch.float64, 524_287, 524_289)])
+def test_noalloc_exact_point_limit_with_unaligned_halves(dtype, N, M):
+    """B*(N+M) exactly at the stated limit, split so that neither key region is a
+    multiple of 256 bytes: accepted, and equal to the workspace entry point; one
+    point more is refused."""
+    x1 = datagen.lidar(N, seed=3, dtype=dtype).to(DEV)
+    x2 = datagen.lidar(M, seed=4, dtype=dtype).to(DEV)
+    got = _noalloc(x1, x2)
+    torch.cuda.synchronize()
+    _same(got, C.chamfer_fwd(x1, x2))
+    x = torch.empty(1, 1, 3, dtype=dtype, device=DEV)
+    rc = C.lib().tpo_chamfer_fwd_noalloc(C.DT[dtype], 0, C.p(x), C.p(x), C.I64(1), C.I64(N),
+                                          C.I64(M + 1), C.p(x), C.p(x), C.p(x), C.p(x), C.stream())
+    assert rc == 3
+
+
+def test_noalloc_rejects_sizes_whose_product_would_wrap():
+    # B*(N+M) wraps a 64-bit size for these values; must be refused, not launched
+    x = torch.empty(1, 1, 3, device=DEV)
+    for B, N, M in [(1 << 40, 1 << 30, 1 << 30), (1 << 62, 4, 4), (3, 1 << 61, 0)]:
+        rc = C.lib().tpo_chamfer_fwd_noalloc(0, 0, C.p(x), C.p(x), C.I64(B), C.I64(N), C.I64(M),
+                                              C.p(x), C.p(x), C.p(x), C.p(x), C.stream())
+        assert rc in (1, 3)  # TPO_ERR_INVALID_ARGUMENT or TPO_ERR_WORKSPACE

@@ -8,16 +8,14 @@ from . import _lib
 from ._lib import get_rounding, set_rounding
 from .chamfer import ChamferDistance, chamfer_distance, chamfer_distance_with_idx, chamfer_loss
 from .knn import KNearestNeighbors, KNNFunction, knn_function, knn_gather, knn_points
-from .fps import (FarthestPointSampling, FPSFunction, PointGatherer, QuickFarthestPointSampling,
-                  QuickFPSFunction, farthest_point_sample_and_gather, furthest_point_sampling,
-                  gather_points, quick_farthest_point_sample_and_gather, quick_furthest_point_sampling)
+from .fps import (FarthestPointSampling, FPSFunction, PointGatherer, farthest_point_sample_and_gather,
+                  furthest_point_sampling, gather_points)
 
 __version__ = "0.1.0"
 __all__ = [
     "chamfer_distance", "chamfer_distance_with_idx", "chamfer_loss", "ChamferDistance",
     "knn_points", "knn_gather", "KNearestNeighbors", "KNNFunction", "knn_function",
     "furthest_point_sampling", "gather_points", "farthest_point_sample_and_gather",
-    "FarthestPointSampling", "PointGatherer", "FPSFunction", "quick_furthest_point_sampling",
-    "quick_farthest_point_sample_and_gather", "QuickFarthestPointSampling", "QuickFPSFunction",
+    "FarthestPointSampling", "PointGatherer", "FPSFunction",
     "set_rounding", "get_rounding",
 ]

@@ -26,7 +26,8 @@ LIB = os.path.join(PKG, "lib")
 CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
 
-CU_SOURCES = ["chamfer_fwd.cu", "chamfer_bwd.cu", "knn.cu", "capi.cu", "chamfer_noalloc.cu", "gather_points.cu", "fps.cu"]
+CU_SOURCES = ["chamfer_fwd.cu", "chamfer_bwd.cu", "knn.cu", "capi.cu", "chamfer_noalloc.cu", "gather_points.cu", "fps.cu",
+              "pipe_probe.cu"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-lineinfo", "-O3", "-std=c++17",

@@ -19,8 +19,9 @@ class ChamferDistance(torch.nn.Module):
         self.reduction = reduction
 
     def forward(self, xyz1, xyz2):
-        # "mean"/"sum": one fused op (the reduction runs inside the finalize kernel
-        # and its gradient scaling inside the backward scatter)
+        # "mean"/"sum": one fused op (the reduction runs in keys_loss_reduce_kernel
+        # right after the keys kernel, and its gradient scaling inside the
+        # backward scatter)
         if self.reduction in ("mean", "sum"):
             return chamfer_loss(xyz1, xyz2, self.reduction)
         return chamfer_distance(xyz1, xyz2)

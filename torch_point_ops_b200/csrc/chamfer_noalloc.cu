@@ -21,9 +21,13 @@
 
 namespace tpo {
 
-// 16 MiB: 2M packed keys for f32/f16 (B*(N+M) <= 2,097,152 points, e.g. two
-// 1M-point clouds), 1M keys for f64.
-constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
+// Limit: B*(N+M) <= 2,097,152 points for f32/f16 (8-byte keys, e.g. two
+// 1M-point clouds), 1,048,576 for f64 (16-byte keys): 16 MiB of keys.  The array
+// holds 512 bytes more because the two key regions each start on a 256-byte
+// boundary (up to 248 bytes of padding each for 8-byte keys), so every problem
+// within the point limit fits whatever the split between N and M.
+constexpr size_t kNoAllocKeyBytes = size_t(16) << 20;
+constexpr size_t kNoAllocScratchBytes = kNoAllocKeyBytes + 512;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 namespace {
@@ -60,14 +64,15 @@ extern "C" TPO_API int tpo_chamfer_fwd_noalloc(int dtype, int flags, const void*
   if (dtype != TPO_F32 && dtype != TPO_F16 && dtype != TPO_F64)
     return set_error(TPO_ERR_INVALID_ARGUMENT, "chamfer_fwd_noalloc: dtype must be f32, f16 or f64");
   if (B < 0 || N < 0 || M < 0) return set_error(TPO_ERR_INVALID_ARGUMENT, "chamfer_fwd_noalloc: negative size");
-  if ((B * N > 0 && (!xyz1 || !dist1 || !idx1)) || (B * M > 0 && (!xyz2 || !dist2 || !idx2)))
-    return set_error(TPO_ERR_INVALID_ARGUMENT, "chamfer_fwd_noalloc: null pointer");
-  const size_t need = tpo_chamfer_fwd_workspace_size(dtype, B, N, M);
-  if (need > kNoAllocScratchBytes)
+  // the point limit, checked without overflow: each factor is bounded first
+  const int64_t max_points = (int64_t)(kNoAllocKeyBytes / (size_t)tpo_chamfer_key_bytes(dtype));
+  if (B > max_points || N > max_points || M > max_points || B * (N + M) > max_points)
     return set_error(TPO_ERR_WORKSPACE,
                      "chamfer_fwd_noalloc: problem too large for the library's 16 MiB scratch "
-                     "(needs 8 B per point for f32/f16, 16 B for f64, over B*(N+M) points); "
+                     "(B*(N+M) must be <= 2,097,152 points for f32/f16, 1,048,576 for f64); "
                      "use tpo_chamfer_fwd with a caller-provided workspace");
+  if ((B * N > 0 && (!xyz1 || !dist1 || !idx1)) || (B * M > 0 && (!xyz2 || !dist2 || !idx2)))
+    return set_error(TPO_ERR_INVALID_ARGUMENT, "chamfer_fwd_noalloc: null pointer");
   void* scratch = nullptr;
   int s = scratch_for_current_device(&scratch);
   if (s) return s;

@@ -1,0 +1,162 @@
+// Arithmetic-pipe peak probe: measures, on the current device, the sustained
+// issue rate of one floating-point instruction kind, so the rooflines of the
+// CUDA-core kernels (chamfer keys, knn) are quoted against a measured peak
+// rather than a datasheet number.
+//
+// Each thread runs 8 independent dependency chains of the instruction (enough
+// instruction-level parallelism to cover its latency at 8 warps per scheduler),
+// over a grid of 4 CTAs x 256 threads per SM.  Result: lane-operations per
+// second (one lane-operation = one element result: a packed x2 instruction on
+// one lane counts 2), and the SM clock during the run from clock64 against
+// %globaltimer on one thread.
+#include <cstdint>
+
+#include "tpo_internal.h"
+
+namespace tpo {
+namespace {
+
+constexpr int kChains = 8;
+constexpr int kIters = 2048;
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+template <int KIND>
+__global__ void __launch_bounds__(256) pipe_probe_kernel(float seed, float* sink,
+                                                         unsigned long long* clk) {
+  uint64_t c0 = 0, t0 = 0;
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    t0 = globaltimer();
+    c0 = clock64();
+  }
+  const float s = seed + threadIdx.x * 1e-7f;
+  if constexpr (KIND == 0) {  // scalar fma.rn.f32
+    float a[kChains];
+#pragma unroll
+    for (int c = 0; c < kChains; ++c) a[c] = s + c;
+    const float m = 0.999999f, k = 1e-7f;
+    for (int i = 0; i < kIters; ++i) {
+#pragma unroll
+      for (int c = 0; c < kChains; ++c) asm volatile("fma.rn.f32 %0, %0, %1, %2;" : "+f"(a[c]) : "f"(m), "f"(k));
+    }
+    float r = 0.f;
+#pragma unroll
+    for (int c = 0; c < kChains; ++c) r += a[c];
+    if (r == 1234.5f) *sink = r;
+  } else if constexpr (KIND == 1) {  // packed fma.rn.f32x2
+    unsigned long long a[kChains];
+#pragma unroll
+    for (int c = 0; c < kChains; ++c) {
+      const float v = s + c;
+      a[c] = ((unsigned long long)__float_as_uint(v) << 32) | __float_as_uint(v + 0.5f);
+    }
+    const unsigned long long m = ((unsigned long long)__float_as_uint(0.999999f) << 32) | __float_as_uint(0.999999f);
+    const unsigned long long k = ((unsigned long long)__float_as_uint(1e-7f) << 32) | __float_as_uint(1e-7f);
+    for (int i = 0; i < kIters; ++i) {
+#pragma unroll
+      for (int c = 0; c < kChains; ++c) asm volatile("fma.rn.f32x2 %0, %0, %1, %2;" : "+l"(a[c]) : "l"(m), "l"(k));
+    }
+    unsigned long long r = 0;
+#pragma unroll
+    for (int c = 0; c < kChains; ++c) r ^= a[c];
+    if (r == 12345ull) *sink = 1.f;
+  } else if constexpr (KIND == 2) {  // packed fma.rn.f16x2
+    unsigned a[kChains];
+#pragma unroll
+    for (int c = 0; c < kChains; ++c) {
+      const __half2 v = __floats2half2_rn(s + c * 0.01f, s);
+      a[c] = *reinterpret_cast<const unsigned*>(&v);
+    }
+    const __half2 mh = __floats2half2_rn(0.999f, 0.999f), kh = __floats2half2_rn(1e-3f, 1e-3f);
+    const unsigned m = *reinterpret_cast<const unsigned*>(&mh), k = *reinterpret_cast<const unsigned*>(&kh);
+    for (int i = 0; i < kIters; ++i) {
+#pragma unroll
+      for (int c = 0; c < kChains; ++c) asm volatile("fma.rn.f16x2 %0, %0, %1, %2;" : "+r"(a[c]) : "r"(m), "r"(k));
+    }
+    unsigned r = 0;
+#pragma unroll
+    for (int c = 0; c < kChains; ++c) r ^= a[c];
+    if (r == 12345u) *sink = 1.f;
+  } else {  // scalar fma.rn.f64
+    double a[kChains];
+#pragma unroll
+    for (int c = 0; c < kChains; ++c) a[c] = (double)s + c;
+    const double m = 0.9999999, k = 1e-9;
+    for (int i = 0; i < kIters; ++i) {
+#pragma unroll
+      for (int c = 0; c < kChains; ++c) asm volatile("fma.rn.f64 %0, %0, %1, %2;" : "+d"(a[c]) : "d"(m), "d"(k));
+    }
+    double r = 0.0;
+#pragma unroll
+    for (int c = 0; c < kChains; ++c) r += a[c];
+    if (r == 1234.5) *sink = (float)r;
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    const uint64_t c1 = clock64(), t1 = globaltimer();
+    clk[0] = c1 - c0;
+    clk[1] = t1 - t0;
+  }
+}
+
+}  // namespace
+
+int pipe_probe(int kind, double* lane_ops_per_s, double* sm_mhz) {
+  using Kern = void (*)(float, float*, unsigned long long*);
+  static const Kern kernels[4] = {pipe_probe_kernel<0>, pipe_probe_kernel<1>, pipe_probe_kernel<2>,
+                                  pipe_probe_kernel<3>};
+  if (kind < 0 || kind > 3) return set_error(TPO_ERR_INVALID_ARGUMENT, "pipe_probe: kind must be 0..3");
+  int dev = 0, sms = 0;
+  int s = cuda_status(cudaGetDevice(&dev));
+  if (!s) s = cuda_status(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  if (s) return s;
+  cudaStream_t st = nullptr;
+  float* sink = nullptr;
+  unsigned long long* clk = nullptr;
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  s = cuda_status(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+  if (!s) s = cuda_status(cudaMalloc(&sink, 16));
+  if (!s) s = cuda_status(cudaMalloc(&clk, 2 * sizeof(unsigned long long)));
+  if (!s) s = cuda_status(cudaEventCreate(&e0));
+  if (!s) s = cuda_status(cudaEventCreate(&e1));
+  const int blocks = sms * 4, threads = 256;
+  float best_ms = 1e30f;
+  unsigned long long hclk[2] = {0, 1};
+  for (int rep = 0; rep < 4 && !s; ++rep) {  // rep 0 warms the clocks up
+    kernels[kind]<<<blocks, threads, 0, st>>>(1.0f, sink, clk);
+    s = check_launch();
+    if (!s) s = cuda_status(cudaEventRecord(e0, st));
+    kernels[kind]<<<blocks, threads, 0, st>>>(1.0f, sink, clk);
+    if (!s) s = check_launch();
+    if (!s) s = cuda_status(cudaEventRecord(e1, st));
+    if (!s) s = cuda_status(cudaEventSynchronize(e1));
+    float ms = 0.f;
+    if (!s) s = cuda_status(cudaEventElapsedTime(&ms, e0, e1));
+    if (!s && rep > 0 && ms < best_ms) {
+      best_ms = ms;
+      s = cuda_status(cudaMemcpy(hclk, clk, sizeof(hclk), cudaMemcpyDeviceToHost));
+    }
+  }
+  if (!s) {
+    const double per_instr = (kind == 1 || kind == 2) ? 2.0 : 1.0;  // element results per lane
+    const double ops = (double)blocks * threads * kIters * kChains * per_instr;
+    *lane_ops_per_s = ops / (best_ms * 1e-3);
+    *sm_mhz = hclk[1] ? (double)hclk[0] / (double)hclk[1] * 1e3 : 0.0;
+  }
+  if (e0) cudaEventDestroy(e0);
+  if (e1) cudaEventDestroy(e1);
+  if (sink) cudaFree(sink);
+  if (clk) cudaFree(clk);
+  if (st) cudaStreamDestroy(st);
+  return s;
+}
+
+}  // namespace tpo
+
+extern "C" int tpo_probe_pipe_peak(int kind, double* lane_ops_per_s, double* sm_mhz) {
+  if (!lane_ops_per_s || !sm_mhz) return tpo::set_error(TPO_ERR_INVALID_ARGUMENT, "pipe_probe: null output");
+  return tpo::pipe_probe(kind, lane_ops_per_s, sm_mhz);
+}

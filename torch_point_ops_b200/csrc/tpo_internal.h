@@ -15,6 +15,7 @@ int cuda_status(cudaError_t e);
 int check_launch();
 // Records `msg` for tpo_status_string and returns `code`.
 int set_error(int code, const char* msg);
+int pipe_probe(int kind, double* lane_ops_per_s, double* sm_mhz);
 
 int chamfer_fwd_keys(int dtype, int flags, const void* x1, const void* x2, int64_t B, int64_t N,
                      int64_t M, int64_t rb0, int64_t rb1, void* k1, void* k2, cudaStream_t st);

@@ -1,11 +1,7 @@
 """Furthest point sampling and gather_points -- drop-in for torch_point_ops.fps
 (torch_point_ops/fps/__init__.py, fps/fps.py): same functions, modules, errors
-and autograd.
-
-``quick_furthest_point_sampling`` keeps the reference's signature and checks
-(fps/__init__.py:205-262) but returns the EXACT furthest point sampling: the
-reference's kd-tree variant (fps/csrc/cuda/quick_fps.cu) is an approximation
-whose output this package does not reproduce."""
+and autograd.  The reference's approximate kd-tree sampler (quick_* names,
+fps/csrc/cuda/quick_fps.cu) is not part of this package."""
 import torch
 
 from .. import _lib
@@ -78,33 +74,9 @@ def farthest_point_sample_and_gather(points: torch.Tensor, nsamples: int):
     return indices, sampled
 
 
-def quick_furthest_point_sampling(points: torch.Tensor, nsamples: int, kd_depth: int = 4) -> torch.Tensor:
-    """The reference's quick-FPS entry point (same arguments and ValueErrors);
-    kd_depth is validated and otherwise unused: the result is the exact FPS."""
-    if points.dim() != 3 or points.shape[2] != 3:
-        raise ValueError(f"Expected points to have shape (N, P, 3), but got {points.shape}")
-    if nsamples <= 0:
-        raise ValueError(f"nsamples must be positive, but got {nsamples}")
-    if nsamples > points.shape[1]:
-        raise ValueError(f"nsamples ({nsamples}) cannot exceed number of points ({points.shape[1]})")
-    if kd_depth <= 0 or kd_depth > 10:
-        raise ValueError(f"kd_depth must be between 1 and 10, but got {kd_depth}")
-    return furthest_point_sampling(points, nsamples)
-
-
-def quick_farthest_point_sample_and_gather(points: torch.Tensor, nsamples: int, kd_depth: int = 4):
-    """(indices, sampled points) of quick_furthest_point_sampling."""
-    indices = quick_furthest_point_sampling(points, nsamples, kd_depth)
-    sampled = gather_points(points.transpose(1, 2), indices).transpose(1, 2)
-    return indices, sampled
-
-
-from .fps import (FarthestPointSampling, FPSFunction, PointGatherer,  # noqa: E402
-                  QuickFarthestPointSampling, QuickFPSFunction, fps_function, quick_fps_function)
+from .fps import FarthestPointSampling, FPSFunction, PointGatherer, fps_function  # noqa: E402
 
 __all__ = [
     "furthest_point_sampling", "gather_points", "farthest_point_sample_and_gather",
-    "quick_furthest_point_sampling", "quick_farthest_point_sample_and_gather",
-    "FarthestPointSampling", "PointGatherer", "FPSFunction", "QuickFarthestPointSampling",
-    "QuickFPSFunction", "fps_function", "quick_fps_function",
+    "FarthestPointSampling", "PointGatherer", "FPSFunction", "fps_function",
 ]

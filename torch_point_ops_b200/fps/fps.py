@@ -1,9 +1,8 @@
 """Module wrappers of furthest point sampling / gather_points
-(torch_point_ops/fps/fps.py: FarthestPointSampling, PointGatherer, FPSFunction,
-QuickFarthestPointSampling, QuickFPSFunction)."""
+(torch_point_ops/fps/fps.py: FarthestPointSampling, PointGatherer, FPSFunction)."""
 import torch
 
-from . import furthest_point_sampling, gather_points, quick_furthest_point_sampling
+from . import furthest_point_sampling, gather_points
 
 
 def _sample(points, nsamples, return_gathered):
@@ -43,38 +42,4 @@ class FPSFunction(torch.nn.Module):
         return _sample(points, nsamples, return_gathered)
 
 
-def _quick(points, nsamples, kd_depth, return_gathered):
-    indices = quick_furthest_point_sampling(points, nsamples, kd_depth)
-    if not return_gathered:
-        return indices
-    sampled = gather_points(points.transpose(1, 2), indices).transpose(1, 2)
-    return indices, sampled
-
-
-class QuickFarthestPointSampling(torch.nn.Module):
-    """The reference's quick-FPS module (same arguments and checks); samples with
-    the exact FPS."""
-
-    def __init__(self, nsamples, kd_depth=4, return_gathered=False):
-        super().__init__()
-        if nsamples <= 0:
-            raise ValueError(f"nsamples must be positive, but got {nsamples}")
-        if kd_depth <= 0 or kd_depth > 10:
-            raise ValueError(f"kd_depth must be between 1 and 10, but got {kd_depth}")
-        self.nsamples = nsamples
-        self.kd_depth = kd_depth
-        self.return_gathered = return_gathered
-
-    def forward(self, points):
-        return _quick(points, self.nsamples, self.kd_depth, self.return_gathered)
-
-
-class QuickFPSFunction(torch.nn.Module):
-    """Functional quick FPS: forward(points, nsamples, kd_depth=4, return_gathered=False)."""
-
-    def forward(self, points, nsamples, kd_depth=4, return_gathered=False):
-        return _quick(points, nsamples, kd_depth, return_gathered)
-
-
 fps_function = FPSFunction()
-quick_fps_function = QuickFPSFunction()

@@ -16,12 +16,7 @@ import torch
 import torch.distributed as dist
 
 from . import _lib
-
-
-def row_range(n: int, world: int, rank: int) -> tuple[int, int]:
-    """Contiguous, balanced [begin, end) share of n items for `rank`."""
-    return (n * rank) // world, (n * (rank + 1)) // world
-
+from .partition import knn_units, row_range
 
 col_range = row_range
 
@@ -77,3 +72,65 @@ def sharded_chamfer_loss(xyz1: torch.Tensor, xyz2: torch.Tensor, group=None, fla
         gx1 = flat[: gx1.numel()].view_as(gx1)
         gx2 = flat[gx1.numel():].view_as(gx2)
     return part.to(xyz1.dtype), gx1, gx2
+
+
+class KnnUnits:
+    """One rank's share of a ragged knn batch, as (batch, query-row range) units
+    balanced by lengths1*lengths2 work over the ranks (partition.knn_units).
+
+    The units are packed into one padded batch (S units, longest unit's rows) by
+    gathers whose index tensors are built once here, so the rank runs ONE
+    knn_points launch over all of its units; autograd carries the gradients back
+    through the gathers into the full (B, P, 3) inputs.  Indices returned by
+    the knn are indices into the unit's own batch of p2, as in the unsplit call."""
+
+    def __init__(self, lengths1, lengths2, world: int, rank: int, device):
+        l1 = [int(v) for v in lengths1]
+        l2 = [int(v) for v in lengths2]
+        self.units = knn_units(l1, l2, world, rank)
+        S = len(self.units)
+        L = max([r1 - r0 for _, r0, r1 in self.units], default=0)
+        b = torch.tensor([u[0] for u in self.units], dtype=torch.int64)
+        r0 = torch.tensor([u[1] for u in self.units], dtype=torch.int64)
+        n = torch.tensor([u[2] - u[1] for u in self.units], dtype=torch.int64)
+        rows = r0[:, None] + torch.arange(L, dtype=torch.int64)[None, :]
+        rows = torch.minimum(rows, (r0 + n - 1).clamp_min(0)[:, None])  # pad rows repeat the last valid one
+        self.batch = b.to(device)
+        self.rows = rows.to(device)
+        self.lengths1 = n.to(device)
+        self.lengths2 = torch.tensor([l2[u[0]] for u in self.units], dtype=torch.int64).to(device)
+        self.work = sum((r1 - r0) * l2[bb] for bb, r0, r1 in self.units)
+
+    def gather(self, p1, p2):
+        """(p1_units (S, L, D), p2_units (S, P2, D)), differentiable gathers."""
+        return p1[self.batch[:, None], self.rows], p2[self.batch]
+
+
+def sharded_knn_loss(p1, p2, units: KnnUnits, K: int, group=None, norm: int = 2):
+    """sum(dists) + sum(nn) of KNearestNeighbors(K, return_nn=True) over the whole
+    ragged batch, computed on this rank's units; returns (loss, grad_p1, grad_p2),
+    identical on every rank after one all_reduce(SUM) of the gradients (the
+    rank's units write disjoint rows of grad_p1 but may share a batch's p2)."""
+    from .knn import knn_gather, knn_points
+
+    a = p1.detach().requires_grad_()
+    b = p2.detach().requires_grad_()
+    if len(units.units):
+        pa, pb = units.gather(a, b)
+        idx, d = knn_points(pa, pb, units.lengths1, units.lengths2, norm=norm, K=K)
+        nn = knn_gather(pb, idx, units.lengths2)
+        # padded rows (beyond the unit's length) carry idx -1 / dist 0 and
+        # gather zero: they add nothing to the loss or the gradients
+        loss = d.sum() + nn.sum()
+        ga, gb = torch.autograd.grad(loss, [a, b])
+        loss = loss.detach()
+    else:
+        loss = torch.zeros((), dtype=p1.dtype, device=p1.device)
+        ga, gb = torch.zeros_like(p1), torch.zeros_like(p2)
+    if dist.is_initialized() and dist.get_world_size(group) > 1:
+        flat = torch.cat([ga.reshape(-1), gb.reshape(-1), loss.reshape(1)])
+        dist.all_reduce(flat, group=group)
+        ga = flat[: ga.numel()].view_as(ga)
+        gb = flat[ga.numel(): ga.numel() + gb.numel()].view_as(gb)
+        loss = flat[-1]
+    return loss, ga, gb
