@@ -205,7 +205,12 @@ def step_fn(cfg, mode="single", units=None, batch_share=1.0):
     """The timed step through the public API.  mode: 'single' (one GPU's whole
     problem, also each rank's problem under --split weak), 'rows' (config 5's
     row-sharded cloud pair), 'strong' (this rank's share of one fixed batched
-    problem: its batches for chamfer, its balanced (batch, row) units for knn)."""
+    problem: its batches for chamfer, its balanced (batch, row) units for knn).
+
+    Returns (step, post): step(*inputs) -> (loss, grad1, grad2) runs the whole
+    step eagerly; `post` is None, or a pair (compute, reduce) that splits a step
+    with a collective into a CUDA-graph-capturable compute part returning one
+    flat buffer and the collective run on that buffer after each replay."""
     import torch_point_ops_b200 as tpo
 
     if mode == "rows":
@@ -213,30 +218,38 @@ def step_fn(cfg, mode="single", units=None, batch_share=1.0):
 
         def sstep(x1, x2):
             return sharded_chamfer_loss(x1.detach(), x2.detach())
-        return sstep
+        return sstep, None
     if mode == "strong" and cfg["kind"] == "knn":
         from torch_point_ops_b200.sharded import sharded_knn_loss
 
+        def compute(p1, p2, l1, l2):
+            loss, ga, gb = sharded_knn_loss(p1, p2, units, cfg["K"], reduce=False)
+            return torch.cat([ga.reshape(-1), gb.reshape(-1), loss.reshape(1)])
+
+        def reduce(flat):
+            torch.distributed.all_reduce(flat)
+            return flat
+
         def kstep_units(p1, p2, l1, l2):
-            return sharded_knn_loss(p1, p2, units, cfg["K"])
-        return kstep_units
+            flat = reduce(compute(p1, p2, l1, l2))
+            n1 = p1.numel()
+            return flat[-1], flat[:n1].view_as(p1), flat[n1:n1 + p2.numel()].view_as(p2)
+        return kstep_units, (compute, reduce)
     if cfg["kind"] == "fps":
         def fstep(x):
             return (tpo.furthest_point_sampling(x, cfg["S"]),)
-        return fstep
+        return fstep, None
     if cfg["kind"] == "chamfer":
         crit = tpo.ChamferDistance("mean")
 
         def step(x1, x2):
-            loss = crit(x1, x2)
+            # strong split: this rank's batches; its loss is its share of the
+            # global mean (the global loss is the sum of the ranks' values, an
+            # optional scalar all-reduce the step does not need)
+            loss = crit(x1, x2) * batch_share if batch_share != 1.0 else crit(x1, x2)
             g1, g2 = torch.autograd.grad(loss, [x1, x2])
-            if mode == "strong":
-                # this rank's batches: the global mean is the batch-weighted sum
-                # of the ranks' means (the optional scalar all-reduce of the loss)
-                loss = loss * batch_share
-                torch.distributed.all_reduce(loss)
             return loss, g1, g2
-        return step
+        return step, None
     knn = tpo.KNearestNeighbors(K=cfg["K"], return_nn=True)
 
     def kstep(p1, p2, l1, l2):
@@ -244,7 +257,7 @@ def step_fn(cfg, mode="single", units=None, batch_share=1.0):
         loss = dists.sum() + nn.sum()
         g1, g2 = torch.autograd.grad(loss, [p1, p2])
         return loss, g1, g2
-    return kstep
+    return kstep, None
 
 
 def launches_per_step(cfg, mode="single"):
@@ -291,11 +304,14 @@ def parity_strong(cfg, step, glob_inputs, mine, dev):
     gradients within 1e-6 relative (atol 1e-9); knn -- the global loss within
     1e-5 relative (float32 sums of 10^6 terms in different orders) and both
     gradients within rtol 1e-5 / atol 1e-6 (fp32 atomics scatter in free order)."""
-    full = step_fn(cfg, "single")
+    full, _ = step_fn(cfg, "single")
     gi = [t.to(dev) for t in glob_inputs]
     gi = [t.requires_grad_() if t.is_floating_point() else t for t in gi]
     rl, r1, r2 = full(*gi)
     ml, m1, m2 = step(*mine)
+    if cfg["kind"] == "chamfer":  # the ranks' loss shares add up to the global mean
+        ml = ml.detach().clone()
+        torch.distributed.all_reduce(ml)
     lerr = abs(float(ml) - float(rl)) / max(abs(float(rl)), 1e-30)
     if cfg["kind"] == "chamfer":
         b0, b1 = mine[0].b_range
@@ -342,7 +358,7 @@ def run_ours(args, cfg):
     diff = [t.requires_grad_() if t.is_floating_point() and cfg["kind"] != "fps" else t for t in inputs]
     if mode == "strong" and cfg["kind"] == "chamfer":
         diff[0].b_range = (b0, b1)
-    step = step_fn(cfg, mode, units=units, batch_share=share)
+    step, post = step_fn(cfg, mode, units=units, batch_share=share)
     flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)  # 256 MiB > L2
 
     parity = None
@@ -364,11 +380,15 @@ def run_ours(args, cfg):
     torch.cuda.current_stream().wait_stream(s)
     torch.cuda.synchronize()
     graph = None
-    if mode == "single":  # steps with NCCL collectives are timed eagerly
+    flat = None
+    if mode != "rows":  # the row-sharded config-5 step (~0.1 s per rank) runs eagerly
         try:
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph):
-                out = step(*diff)
+                if post is None:
+                    out = step(*diff)
+                else:  # the compute part only; its collective runs after each replay
+                    flat = post[0](*diff)
         except Exception as e:  # capture unsupported -> eager (reported)
             graph = None
             print(f"[bench] graph capture failed ({e}); timing eager steps", file=sys.stderr)
@@ -376,6 +396,8 @@ def run_ours(args, cfg):
     def run_step():
         if graph is not None:
             graph.replay()
+            if post is not None:
+                post[1](flat)
         else:
             step(*diff)
 
@@ -425,7 +447,7 @@ def run_ours(args, cfg):
     e2e_pipe = run_e2e_pipelined(args, cfg, step, host_inputs, dev, ws)
     e2e_pipe_value = pairs * jobs / (e2e_pipe["ms"] * 1e-3) / 1e9
     e2e_graph = e2e_gp = None
-    if mode == "single" and not big:
+    if post is None and mode != "rows" and not big:
         try:
             e2e_graph = run_e2e_pipelined(args, cfg, step, host_inputs, dev, ws, graphs=True)
         except Exception as e:  # capture unsupported -> reported as absent
@@ -442,7 +464,7 @@ def run_ours(args, cfg):
     if cfg["kind"] != "fps":
         try:
             e2e_grads = (run_e2e_graph_pipeline(args, cfg, step, host_inputs, dev, ws, grads=True)
-                         if mode == "single" and not big else
+                         if post is None and mode != "rows" and not big else
                          run_e2e_pipelined(args, cfg, step, host_inputs, dev, ws, grads=True))
             e2e_grads["value"] = pairs * jobs / (e2e_grads["ms"] * 1e-3) / 1e9
         except Exception as e:

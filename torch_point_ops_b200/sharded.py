@@ -106,11 +106,14 @@ class KnnUnits:
         return p1[self.batch[:, None], self.rows], p2[self.batch]
 
 
-def sharded_knn_loss(p1, p2, units: KnnUnits, K: int, group=None, norm: int = 2):
+def sharded_knn_loss(p1, p2, units: KnnUnits, K: int, group=None, norm: int = 2,
+                     reduce: bool = True):
     """sum(dists) + sum(nn) of KNearestNeighbors(K, return_nn=True) over the whole
     ragged batch, computed on this rank's units; returns (loss, grad_p1, grad_p2),
     identical on every rank after one all_reduce(SUM) of the gradients (the
-    rank's units write disjoint rows of grad_p1 but may share a batch's p2)."""
+    rank's units write disjoint rows of grad_p1 but may share a batch's p2).
+    reduce=False returns this rank's partial sums without the collective (for a
+    caller that captures the compute in a CUDA graph and reduces after it)."""
     from .knn import knn_gather, knn_points
 
     a = p1.detach().requires_grad_()
@@ -127,7 +130,7 @@ def sharded_knn_loss(p1, p2, units: KnnUnits, K: int, group=None, norm: int = 2)
     else:
         loss = torch.zeros((), dtype=p1.dtype, device=p1.device)
         ga, gb = torch.zeros_like(p1), torch.zeros_like(p2)
-    if dist.is_initialized() and dist.get_world_size(group) > 1:
+    if reduce and dist.is_initialized() and dist.get_world_size(group) > 1:
         flat = torch.cat([ga.reshape(-1), gb.reshape(-1), loss.reshape(1)])
         dist.all_reduce(flat, group=group)
         ga = flat[: ga.numel()].view_as(ga)
