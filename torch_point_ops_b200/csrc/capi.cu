@@ -49,10 +49,11 @@ const char* tpo_status_string(int status) {
 
 int tpo_device_error_flags(unsigned* flags, int clear) {
   if (!flags) return fail(TPO_ERR_INVALID_ARGUMENT, "device_error_flags: null output");
-  unsigned a = 0, b = 0;
+  unsigned a = 0, b = 0, c = 0;
   int s = device_error_flags(&a, clear != 0);
   if (!s) s = fps_device_error_flags(&b, clear != 0);
-  *flags = a | b;
+  if (!s) s = knn_device_error_flags(&c, clear != 0);
+  *flags = a | b | c;
   return s;
 }
 

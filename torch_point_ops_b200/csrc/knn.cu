@@ -256,6 +256,213 @@ __global__ void __launch_bounds__(KW * 32)
   }
 }
 
+// fp32, D=3, squared L2 (the benchmark's knn case): the same warp-distributed
+// top-K lists, with the per-target work cut to the arithmetic plus one packed
+// op of filtering:
+//   * target tiles land by 1-D bulk copies (TMA) into two shared buffers: the
+//     copy of tile t+1 runs while tile t is scanned, so no warp waits on a load;
+//     a lane reads its target's x,y,z and forms the {c,c} pairs in registers;
+//   * the filter is ONE packed subtraction per query pair, d - thr: for floats
+//     fl(d - thr) is negative exactly when d < thr (distinct floats never
+//     subtract to zero), +inf thresholds pass everything, the -inf threshold of
+//     an invalid query slot and the NaN padding pass nothing -- so the pass
+//     bits are sign bits, OR-ed across queries with logic ops;
+//   * KS steps share one warp vote; only then do the per-query ballots and
+//     insertions run (in step order, each candidate re-checked against the
+//     current threshold, so candidates still arrive in increasing index order).
+static __device__ unsigned g_knn_device_error = 0;
+#ifndef TPO_KT3
+#define TPO_KT3 1024
+#endif
+constexpr int KT3 = TPO_KT3;  // targets per tile (two tiles in shared memory)
+
+template <int KQF, int KS>
+__global__ void __launch_bounds__(KW * 32)
+    knn_fwd_f32x3_kernel(const float* __restrict__ p1, const float* __restrict__ p2,
+                         const int64_t* __restrict__ len1, const int64_t* __restrict__ len2,
+                         int64_t N, int64_t P1, int64_t P2, int K, int qblocks,
+                         float* __restrict__ dists, int64_t* __restrict__ idxs) {
+  static_assert(KT3 % (KSTEP * KS) == 0 && KQF % 2 == 0, "tile/step shape");
+  __shared__ __align__(16) float s_raw[2][KT3 * 3];
+  __shared__ __align__(8) unsigned long long s_bar[2];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t n = blockIdx.x / qblocks;
+  const int64_t blk_q0 = (int64_t)(blockIdx.x % qblocks) * (KW * KQF);
+  const int64_t q0 = blk_q0 + warp * KQF;
+  const int64_t L1 = len1 ? min64(max64(len1[n], 0), P1) : P1;
+  const int64_t L2 = len2 ? min64(max64(len2[n], 0), P2) : P2;
+  const float qnan = __int_as_float(0x7fffffff);
+  if (blk_q0 >= L1) {  // no valid query in this CTA: padding rows only
+    if (lane < K)
+      for (int i = 0; i < KQF; ++i) {
+        const int64_t row = q0 + i;
+        if (row >= P1) break;
+        dists[(n * P1 + row) * K + lane] = 0.f;
+        idxs[(n * P1 + row) * K + lane] = -1;
+      }
+    return;
+  }
+
+  u64 QP[KQF / 2][3], THR[KQF / 2];
+  float thr[KQF], Ld[KQF];
+  int Li[KQF];
+  bool qv[KQF];
+#pragma unroll
+  for (int i = 0; i < KQF; ++i) {
+    qv[i] = q0 + i < L1;
+    thr[i] = qv[i] ? __int_as_float(0x7f800000) : __int_as_float(0xff800000);
+    Ld[i] = __int_as_float(0x7f800000);
+    Li[i] = -1;
+  }
+#pragma unroll
+  for (int ip = 0; ip < KQF / 2; ++ip) {
+    THR[ip] = pk(thr[2 * ip], thr[2 * ip + 1]);
+#pragma unroll
+    for (int d = 0; d < 3; ++d) {
+      const float a = qv[2 * ip] ? p1[(n * P1 + q0 + 2 * ip) * 3 + d] : 0.f;
+      const float c = qv[2 * ip + 1] ? p1[(n * P1 + q0 + 2 * ip + 1) * 3 + d] : 0.f;
+      QP[ip][d] = pk(a, c);
+    }
+  }
+  const bool any_q = q0 < L1;
+  const int ntiles = (int)((L2 + KT3 - 1) / KT3);
+  if (threadIdx.x == 0) {
+    mbar_init(&s_bar[0], 1);
+    mbar_init(&s_bar[1], 1);
+  }
+  __syncthreads();
+  // start tile t's copy into buffer t & 1: the 16-byte aligned body by one bulk
+  // copy, the rest (and NaN padding up to whole vote batches) by plain accesses
+  auto issue = [&](int t) {
+    const int64_t t0 = (int64_t)t * KT3;
+    const int nt = (int)min64(KT3, L2 - t0);
+    const int padded = (nt + KSTEP * KS - 1) / (KSTEP * KS) * (KSTEP * KS);
+    const float* src = p2 + (n * P2 + t0) * 3;
+    float* dst = s_raw[t & 1];
+    const int nfl = nt * 3;
+    const int bulk = (((uintptr_t)src & 15) == 0) ? (nfl & ~3) : 0;
+    if (threadIdx.x == 0) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      mbar_expect_tx(&s_bar[t & 1], (unsigned)bulk * 4u);
+      if (bulk) bulk_g2s(dst, src, (unsigned)bulk * 4u, &s_bar[t & 1]);
+    }
+    for (int e = bulk + threadIdx.x; e < padded * 3; e += blockDim.x) dst[e] = e < nfl ? __ldg(src + e) : qnan;
+  };
+  unsigned phase[2] = {0u, 0u};
+  issue(0);
+  if (ntiles > 1) issue(1);
+  for (int t = 0; t < ntiles; ++t) {
+    const int b = t & 1;
+    const int64_t t0 = (int64_t)t * KT3;
+    const int nt = (int)min64(KT3, L2 - t0);
+    const int nbat = (nt + KSTEP * KS - 1) / (KSTEP * KS);
+    mbar_wait(&s_bar[b], phase[b], &g_knn_device_error);
+    phase[b] ^= 1u;
+    __syncthreads();  // plain-loaded elements and padding visible too
+    if (any_q) {
+      const float* tile = s_raw[b];
+#pragma unroll 1
+      for (int bt = 0; bt < nbat; ++bt) {
+        float dv[KS][KQF];
+        u64 sg[KS][KQF / 2];
+        unsigned acc = 0;
+#pragma unroll
+        for (int st = 0; st < KS; ++st) {
+          const float* cp = tile + ((bt * KS + st) * KSTEP + lane) * 3;
+          const float cx = cp[0], cy = cp[1], cz = cp[2];
+          const u64 CX = pk(cx, cx), CY = pk(cy, cy), CZ = pk(cz, cz);
+#pragma unroll
+          for (int ip = 0; ip < KQF / 2; ++ip) {
+            // packed fp32x2 sub/mul for two queries; scalar .rn adds (never
+            // fused): ((dx*dx + dy*dy) + dz*dz), every operation rounded
+            const u64 dx = sub2(QP[ip][0], CX), dy = sub2(QP[ip][1], CY), dz = sub2(QP[ip][2], CZ);
+            float x0, x1, y0, y1, z0, z1;
+            upk(mul2(dx, dx), x0, x1);
+            upk(mul2(dy, dy), y0, y1);
+            upk(mul2(dz, dz), z0, z1);
+            dv[st][2 * ip] = __fadd_rn(__fadd_rn(x0, y0), z0);
+            dv[st][2 * ip + 1] = __fadd_rn(__fadd_rn(x1, y1), z1);
+            sg[st][ip] = sub2(pk(dv[st][2 * ip], dv[st][2 * ip + 1]), THR[ip]);
+            acc |= (unsigned)sg[st][ip] | (unsigned)(sg[st][ip] >> 32);
+          }
+        }
+        if (__any_sync(0xffffffffu, (int)acc < 0)) {
+#pragma unroll
+          for (int st = 0; st < KS; ++st) {
+            const int cbase = (int)t0 + (bt * KS + st) * KSTEP;
+            unsigned bals[KQF];  // all ballots first: independent, issued back to back
+#pragma unroll
+            for (int i = 0; i < KQF; ++i) {
+              const unsigned w = (i & 1) ? (unsigned)(sg[st][i >> 1] >> 32) : (unsigned)sg[st][i >> 1];
+              bals[i] = __ballot_sync(0xffffffffu, (int)w < 0);
+            }
+#pragma unroll
+            for (int i = 0; i < KQF; ++i) {
+              unsigned bal = bals[i];
+              bool changed = false;
+              while (bal) {
+                const int src = __ffs(bal) - 1;
+                bal &= bal - 1;
+                // the list spans all 32 lanes: a candidate that passed the
+                // (possibly stale) filter but not the current K-th entry lands
+                // in a lane >= K and never reaches the output, so no per-
+                // candidate threshold re-check is needed
+                const float cd = __shfl_sync(0xffffffffu, dv[st][i], src);
+                const float upd = __shfl_up_sync(0xffffffffu, Ld[i], 1);
+                const int upi = __shfl_up_sync(0xffffffffu, Li[i], 1);
+                if (cd < Ld[i]) {
+                  const bool take_prev = lane > 0 && cd < upd;
+                  Ld[i] = take_prev ? upd : cd;
+                  Li[i] = take_prev ? upi : cbase + src;
+                }
+                changed = true;
+              }
+              if (changed) {
+                thr[i] = __shfl_sync(0xffffffffu, Ld[i], K - 1);
+                THR[i >> 1] = pk(thr[i & ~1], thr[i | 1]);
+              }
+            }
+          }
+        }
+      }
+    }
+    __syncthreads();  // buffer b free
+    if (t + 2 < ntiles) issue(t + 2);
+  }
+  if (lane < K) {
+#pragma unroll
+    for (int i = 0; i < KQF; ++i) {
+      const int64_t row = q0 + i;
+      if (row >= P1) break;
+      const int64_t o = (n * P1 + row) * K + lane;
+      const bool ok = qv[i] && Li[i] >= 0;
+      dists[o] = ok ? Ld[i] : 0.f;
+      idxs[o] = ok ? (int64_t)Li[i] : -1;
+    }
+  }
+}
+
+#ifndef TPO_KQF
+#define TPO_KQF 4
+#endif
+#ifndef TPO_KS
+#define TPO_KS 1
+#endif
+
+static int launch_knn_f32x3(const float* p1, const float* p2, const int64_t* l1, const int64_t* l2,
+                            int64_t N, int64_t P1, int64_t P2, int K, float* dists, int64_t* idxs,
+                            cudaStream_t st) {
+  constexpr int Q = TPO_KQF;
+  constexpr int S = TPO_KS;
+  const int qblocks = (int)((P1 + KW * Q - 1) / (KW * Q));
+  const int64_t ctas = N * qblocks;
+  if (ctas <= 0) return TPO_OK;
+  knn_fwd_f32x3_kernel<Q, S><<<(unsigned)ctas, KW * 32, 0, st>>>(p1, p2, l1, l2, N, P1, P2, K, qblocks,
+                                                             dists, idxs);
+  return check_launch();
+}
+
 template <typename T, int DT, int NORM, int MODE>
 static int launch_knn_fwd(const T* p1, const T* p2, const int64_t* l1, const int64_t* l2, int64_t N,
                           int64_t P1, int64_t P2, int D, int K, T* dists, int64_t* idxs,
@@ -275,6 +482,10 @@ static int dispatch_knn_fwd(const void* p1, const void* p2, const int64_t* l1, c
   const T* a = (const T*)p1;
   const T* b = (const T*)p2;
   T* o = (T*)dists;
+  if constexpr (std::is_same<T, float>::value) {
+    if (D == 3 && norm == 2)
+      return launch_knn_f32x3(a, b, l1, l2, N, P1, P2, (int)K, o, idxs, st);
+  }
   if (D == 3)
     return norm == 2 ? launch_knn_fwd<T, 3, 2, MODE>(a, b, l1, l2, N, P1, P2, 3, (int)K, o, idxs, st)
                      : launch_knn_fwd<T, 3, 1, MODE>(a, b, l1, l2, N, P1, P2, 3, (int)K, o, idxs, st);
@@ -718,6 +929,13 @@ int knn_gather_backward(int dtype, const void* gout, const int64_t* idx, const i
                         int64_t N, int64_t M, int64_t U, int64_t L, int64_t K, void* gx,
                         cudaStream_t st) {
   return gather_dispatch(true, dtype, gout, idx, lengths, N, M, U, L, K, gx, st);
+}
+
+int knn_device_error_flags(unsigned* out, bool clear) {
+  int s = cuda_status(cudaMemcpyFromSymbol(out, g_knn_device_error, sizeof(unsigned)));
+  if (s || !clear) return s;
+  const unsigned zero = 0;
+  return cuda_status(cudaMemcpyToSymbol(g_knn_device_error, &zero, sizeof(unsigned)));
 }
 
 }  // namespace tpo

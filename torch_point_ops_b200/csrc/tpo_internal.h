@@ -74,6 +74,7 @@ size_t fps_workspace_size(int dtype, int64_t B, int64_t P);
 int fps_forward(int dtype, const void* pts, int64_t B, int64_t P, int64_t S, int64_t* idx,
                 void* ws, size_t ws_bytes, cudaStream_t st);
 int fps_device_error_flags(unsigned* out, bool clear);
+int knn_device_error_flags(unsigned* out, bool clear);
 int gather_points_forward(int dtype, const void* pts, const int64_t* idx, int64_t N, int64_t C,
                           int64_t P, int64_t M, void* out, cudaStream_t st);
 int gather_points_backward(int dtype, const void* gout, const int64_t* idx, int64_t N, int64_t C,
