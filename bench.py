@@ -301,7 +301,7 @@ def parity_rows(dev, ws):
 def parity_strong(cfg, step, glob_inputs, mine, dev):
     """--split strong vs the whole problem on one GPU (run on every rank):
     chamfer -- the global loss within 1e-6 relative and this rank's batches'
-    gradients within 1e-6 relative (atol 1e-9); knn -- the global loss within
+    gradients within the free-order summation bound; knn -- the global loss within
     1e-5 relative (float32 sums of 10^6 terms in different orders) and both
     gradients within rtol 1e-5 / atol 1e-6 (fp32 atomics scatter in free order)."""
     full, _ = step_fn(cfg, "single")
@@ -314,10 +314,24 @@ def parity_strong(cfg, step, glob_inputs, mine, dev):
         torch.distributed.all_reduce(ml)
     lerr = abs(float(ml) - float(rl)) / max(abs(float(rl)), 1e-30)
     if cfg["kind"] == "chamfer":
+        # gradients within twice the per-element bound of tests/tolerances.py
+        # (both sides scatter with atomics in a free order)
+        import numpy as np
+
+        import torch_point_ops_b200 as tpo
+        from tolerances import term_scale, tolerance
         b0, b1 = mine[0].b_range
-        ok = (lerr <= 1e-6 and torch.allclose(m1, r1[b0:b1], rtol=1e-6, atol=1e-9)
-              and torch.allclose(m2, r2[b0:b1], rtol=1e-6, atol=1e-9))
-        err = float(max((m1 - r1[b0:b1]).abs().max(), (m2 - r2[b0:b1]).abs().max()))
+        x1, x2 = mine[0].detach(), mine[1].detach()
+        _, _, i1, i2 = tpo.chamfer_distance_with_idx(x1, x2)
+        B = cfg["B"]
+        g1 = torch.full(i1.shape, 1.0 / (B * x1.shape[1]))
+        g2 = torch.full(i2.shape, 1.0 / (B * x2.shape[1]))
+        s1, s2, n1, n2 = term_scale(x1.cpu(), x2.cpu(), i1.cpu(), i2.cpu(), g1, g2)
+        e1 = np.abs(m1.cpu().double().numpy() - r1[b0:b1].cpu().double().numpy())
+        e2 = np.abs(m2.cpu().double().numpy() - r2[b0:b1].cpu().double().numpy())
+        ok = (lerr <= 1e-6 and bool(np.all(e1 <= 2 * tolerance(torch.float32, s1, n1)))
+              and bool(np.all(e2 <= 2 * tolerance(torch.float32, s2, n2))))
+        err = float(max(e1.max(), e2.max()))
     else:
         ok = (lerr <= 1e-5 and torch.allclose(m1, r1, rtol=1e-5, atol=1e-6)
               and torch.allclose(m2, r2, rtol=1e-5, atol=1e-6))

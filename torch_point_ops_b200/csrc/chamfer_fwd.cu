@@ -486,14 +486,11 @@ __global__ void __launch_bounds__(CF_MAXW * 32, TPO_CF_MINB)
   pdl_trigger();  // the next kernel may be scheduled (it waits for this grid)
 }
 
-// ------------------------- fp16 / fp64 generic path -------------------------
-// Same decomposition with scalar arithmetic: R = 8 rows per lane.
+// ------------------------- scalar distance helpers -------------------------
+// Rescan widths of the fp64 keys in finalize: the keys carry exact indices, so
+// a scan from the key's index finds it first.
 constexpr int CG_R = 8;
 constexpr int CG_C = 4;
-constexpr int CG_TILE_STEPS = 64;
-constexpr int CG_TILE = CG_TILE_STEPS * CG_C;
-constexpr int CG_MAXW = 4;
-constexpr int CG_ROWS_PER_WARP = 32 * CG_R;
 
 template <typename T, int MODE>
 struct GenDist;
@@ -514,70 +511,46 @@ struct GenDist<double, MODE> {
   __device__ static double nan_() { return __longlong_as_double(0x7fffffffffffffffll); }
 };
 
-// Key handling for the two value types.
-template <typename V>
-struct KeyOps;
-template <>
-struct KeyOps<float> {
-  using K = u64;
-  __device__ static K make(float v, unsigned chunk) {
-    return ((u64)__float_as_uint(v) << 32) | chunk;
-  }
-  __device__ static K kmin(K a, K b) { return a < b ? a : b; }
-  __device__ static K empty() { return ~0ull; }
-  __device__ static void flush(K* dst, K k) { red_min_u64(dst, k); }
-  // warp argmin of v (>= 0 or NaN): returns min bit pattern key's value and lowest lane
-  __device__ static void warp_argmin(float v, float& wv, int& win) {
-    const unsigned u = __float_as_uint(v);
-    const unsigned w = redux_min_u32(u);
-    win = __ffs(__ballot_sync(0xffffffffu, u == w)) - 1;
-    wv = __uint_as_float(w);
-  }
-};
-template <>
-struct KeyOps<double> {
-  using K = Key128;
-  __device__ static K make(double v, unsigned chunk) {
-    K k;
-    k.hi = (u64)__double_as_longlong(v);
-    k.lo = chunk;
-    return k;
-  }
-  __device__ static K kmin(K a, K b) { return key128_less(b.hi, b.lo, a.hi, a.lo) ? b : a; }
-  __device__ static K empty() {
-    K k;
-    k.hi = ~0ull;
-    k.lo = ~0ull;
-    return k;
-  }
-  __device__ static void flush(K* dst, K k) { key128_min(dst, k.hi, k.lo); }
-  __device__ static void warp_argmin(double v, double& wv, int& win) {
-    const u64 u = (u64)__double_as_longlong(v);
-    const unsigned hi = (unsigned)(u >> 32);
-    const unsigned whi = redux_min_u32(hi);
-    const unsigned lo = (hi == whi) ? (unsigned)u : 0xffffffffu;
-    const unsigned wlo = redux_min_u32(lo);
-    const u64 w = ((u64)whi << 32) | wlo;
-    win = __ffs(__ballot_sync(0xffffffffu, u == w)) - 1;
-    wv = __longlong_as_double((long long)w);
-  }
-};
+// ----------------------------- fp64 fast path -----------------------------
+// The fp32 kernel's structure for doubles, with the minima tracked on the
+// distances' HIGH 32-bit words.  For d >= 0 the high word (sign, exponent, 20
+// mantissa bits) is monotone in d, so integer minima of high words (3-input
+// vimin3, on the integer pipe) keep the FP64 pipe for the distance itself
+// (3 sub + 1 mul + 2 fma per pair).  The high word is only a proxy; exactness
+// is restored before anything leaves the CTA:
+//   * rows: the 4-column chunk where a row's high-word minimum was first reached
+//     is rescanned in full precision at the end; if a later chunk reached the
+//     SAME high word (a "tie", where a smaller low word could hide) the row's
+//     whole column segment is rescanned instead;
+//   * columns: every lane whose minimum high word equals the warp's minimum is
+//     a candidate (the ballot), every warp whose minimum equals the CTA's is a
+//     candidate, and the merge rescans all candidate lanes' rows in full
+//     precision (usually exactly one lane).
+// Rescans use the identical arithmetic, so the keys are exact (distance bits,
+// lowest index) before the 128-bit atomic merge across CTAs.
+#ifndef TPO_CD_R
+#define TPO_CD_R 8
+#endif
+constexpr int CD_R = TPO_CD_R;   // rows per lane
+constexpr int CD_C = 4;          // columns per step (= the row chunk)
+constexpr int CD_TILE = 256;
+constexpr int CD_W = 4;
+constexpr int CD_ROWS_PER_WARP = 32 * CD_R;
 
-template <typename T, int MODE>
-__global__ void __launch_bounds__(CG_MAXW * 32)
-    chamfer_keys_generic_kernel(const T* __restrict__ xyz1, const T* __restrict__ xyz2,
-                                int64_t N, int64_t M, int64_t row_begin, int64_t row_end,
-                                int rb_count, int cs_count, int64_t seg,
-                                typename KeyOps<typename GenDist<T, MODE>::V>::K* __restrict__ keys1,
-                                typename KeyOps<typename GenDist<T, MODE>::V>::K* __restrict__ keys2) {
-  using G = GenDist<T, MODE>;
-  using V = typename G::V;
-  using KO = KeyOps<V>;
-  using K = typename KO::K;
-  __shared__ __align__(16) T s_col[CG_TILE_STEPS][3][CG_C];
-  __shared__ __align__(16) K s_key[CG_MAXW][CG_TILE];
+__device__ __forceinline__ unsigned hiword(double d) { return (unsigned)__double2hiint(d); }
 
-  pdl_wait();  // launched with programmatic serialisation: inputs/keys ready after this
+template <int MODE>
+__global__ void __launch_bounds__(CD_W * 32, 2)
+    chamfer_keys_f64_kernel(const double* __restrict__ xyz1, const double* __restrict__ xyz2,
+                            int64_t N, int64_t M, int64_t row_begin, int64_t row_end,
+                            int rb_count, int cs_count, int64_t seg, Key128* __restrict__ keys1,
+                            Key128* __restrict__ keys2) {
+  using G = GenDist<double, MODE>;
+  __shared__ __align__(16) double s_rows[CD_W * CD_ROWS_PER_WARP * 3];
+  __shared__ __align__(16) double s_col[CD_TILE][3];
+  __shared__ uint2 s_wb[CD_W][CD_TILE];  // {ballot, minimum high word}
+
+  pdl_wait();
   const int W = blockDim.x >> 5;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -588,88 +561,131 @@ __global__ void __launch_bounds__(CG_MAXW * 32)
   const int64_t b = unit / rb_count;
   const int64_t c0 = (int64_t)cs * seg;
   const int64_t c1 = min(M, c0 + seg);
-  const int64_t blk_row0 = row_begin + (int64_t)rb * W * CG_ROWS_PER_WARP;
-  const int64_t warp_row0 = blk_row0 + (int64_t)warp * CG_ROWS_PER_WARP;
-  const int64_t lane_row0 = warp_row0 + (int64_t)lane * CG_R;
+  const int64_t blk_row0 = row_begin + (int64_t)rb * W * CD_ROWS_PER_WARP;
+  const int64_t warp_row0 = blk_row0 + (int64_t)warp * CD_ROWS_PER_WARP;
+  const int lrow0 = warp * CD_ROWS_PER_WARP + lane * CD_R;  // first row of the lane in s_rows
   const bool warp_active = warp_row0 < row_end;
-  const int n_active = (int)min64(W, (row_end - blk_row0 + CG_ROWS_PER_WARP - 1) / CG_ROWS_PER_WARP);
-
-  T qx[CG_R], qy[CG_R], qz[CG_R];
+  const int n_active = (int)min64(W, (row_end - blk_row0 + CD_ROWS_PER_WARP - 1) / CD_ROWS_PER_WARP);
+  const double qnan = G::nan_();
+  const int64_t nrow = min64((int64_t)W * CD_ROWS_PER_WARP, max64(row_end - blk_row0, 0));
+  for (int e = threadIdx.x; e < W * CD_ROWS_PER_WARP * 3; e += blockDim.x)
+    s_rows[e] = e < nrow * 3 ? __ldg(xyz1 + (b * N + blk_row0) * 3 + e) : qnan;
+  __syncthreads();
+  double qx[CD_R], qy[CD_R], qz[CD_R];
 #pragma unroll
-  for (int r = 0; r < CG_R; ++r) {
-    const bool ok = lane_row0 + r < row_end;
-    const T* a = xyz1 + (b * N + lane_row0 + r) * 3;
-    qx[r] = ok ? a[0] : G::nan_();
-    qy[r] = ok ? a[1] : G::nan_();
-    qz[r] = ok ? a[2] : G::nan_();
+  for (int r = 0; r < CD_R; ++r) {
+    qx[r] = s_rows[(lrow0 + r) * 3];
+    qy[r] = s_rows[(lrow0 + r) * 3 + 1];
+    qz[r] = s_rows[(lrow0 + r) * 3 + 2];
   }
-  V best[CG_R];
-  int bchunk[CG_R];
+  unsigned mh[CD_R];
+  int bchunk[CD_R];
+  unsigned ties = 0;  // bit r: a later chunk reached row r's minimum high word
 #pragma unroll
-  for (int r = 0; r < CG_R; ++r) {
-    best[r] = (V)INFINITY;
-    bchunk[r] = 0;
+  for (int r = 0; r < CD_R; ++r) {
+    mh[r] = 0xffffffffu;
+    bchunk[r] = (int)c0;
   }
 
-  for (int64_t tc = c0; tc < c1; tc += CG_TILE) {
-    const int ncols = (int)min64(CG_TILE, c1 - tc);
-    const int nsteps = (ncols + CG_C - 1) / CG_C;
+  for (int64_t tc = c0; tc < c1; tc += CD_TILE) {
+    const int ncols = (int)min64(CD_TILE, c1 - tc);
+    const int nsteps = (ncols + CD_C - 1) / CD_C;
     __syncthreads();
-    {
-      const T* src = xyz2 + (b * M + tc) * 3;
-      T* dst = &s_col[0][0][0];
-      for (int e = threadIdx.x; e < nsteps * CG_C * 3; e += blockDim.x) {
-        const int col = e / 3;
-        const int comp = e - col * 3;
-        dst[((col >> 2) * 3 + comp) * CG_C + (col & 3)] = col < ncols ? src[e] : G::nan_();
-      }
-    }
+    for (int e = threadIdx.x; e < nsteps * CD_C * 3; e += blockDim.x)
+      (&s_col[0][0])[e] = e < ncols * 3 ? __ldg(xyz2 + (b * M + tc) * 3 + e) : qnan;
     __syncthreads();
     if (warp_active) {
-#pragma unroll 1
+#pragma unroll 2
       for (int s = 0; s < nsteps; ++s) {
-        V d[CG_C][CG_R];
+        unsigned h[CD_C][CD_R];
 #pragma unroll
-        for (int c = 0; c < CG_C; ++c) {
-          const T cx = s_col[s][0][c], cy = s_col[s][1][c], cz = s_col[s][2][c];
+        for (int c = 0; c < CD_C; ++c) {
+          const double cx = s_col[s * CD_C + c][0], cy = s_col[s * CD_C + c][1], cz = s_col[s * CD_C + c][2];
 #pragma unroll
-          for (int r = 0; r < CG_R; ++r) d[c][r] = G::d(cx, cy, cz, qx[r], qy[r], qz[r]);
+          for (int r = 0; r < CD_R; ++r) h[c][r] = hiword(G::d(cx, cy, cz, qx[r], qy[r], qz[r]));
         }
-        const int colbase = (int)(tc + s * CG_C);
+        const int colbase = (int)(tc + s * CD_C);
 #pragma unroll
-        for (int r = 0; r < CG_R; ++r) {
-          const V nb = fmin(fmin(best[r], fmin(d[0][r], d[1][r])), fmin(d[2][r], d[3][r]));
-          if (nb < best[r]) bchunk[r] = colbase;
-          best[r] = nb;
+        for (int r = 0; r < CD_R; ++r) {
+          const unsigned cm = __vimin3_u32(__vimin3_u32(h[0][r], h[1][r], h[2][r]), h[3][r], 0xffffffffu);
+          if (cm < mh[r]) {
+            mh[r] = cm;
+            bchunk[r] = colbase;
+            ties &= ~(1u << r);
+          } else if (cm == mh[r]) {
+            ties |= 1u << r;
+          }
         }
 #pragma unroll
-        for (int c = 0; c < CG_C; ++c) {
-          V m = d[c][0];
+        for (int c = 0; c < CD_C; ++c) {
+          unsigned m = h[c][0];
 #pragma unroll
-          for (int r = 1; r < CG_R; ++r) m = fmin(m, d[c][r]);
-          V wv;
-          int win;
-          KO::warp_argmin(m, wv, win);
-          if (lane == 0)
-            s_key[warp][s * CG_C + c] = KO::make(wv, (unsigned)(warp_row0 + (int64_t)win * CG_R));
+          for (int r = 1; r + 1 < CD_R; r += 2) m = __vimin3_u32(m, h[c][r], h[c][r + 1]);
+          if (CD_R % 2 == 0) m = min(m, h[c][CD_R - 1]);
+          const unsigned w = redux_min_u32(m);
+          const unsigned bal = __ballot_sync(0xffffffffu, m == w);
+          if (lane == 0) s_wb[warp][s * CD_C + c] = make_uint2(bal, w);
         }
       }
     }
     __syncthreads();
+    // column merge: exact over every candidate lane (usually one)
     for (int col = threadIdx.x; col < ncols; col += blockDim.x) {
-      K k = s_key[0][col];
-      for (int w = 1; w < n_active; ++w) k = KO::kmin(k, s_key[w][col]);
-      KO::flush(keys2 + b * M + tc + col, k);
+      unsigned bw = s_wb[0][col].y;
+      for (int w = 1; w < n_active; ++w) bw = min(bw, s_wb[w][col].y);
+      const double cx = s_col[col][0], cy = s_col[col][1], cz = s_col[col][2];
+      double bd = qnan;
+      int brow = -1;
+      for (int w = 0; w < n_active; ++w) {
+        if (s_wb[w][col].y != bw) continue;
+        unsigned bal = s_wb[w][col].x;
+        while (bal) {
+          const int ln = __ffs(bal) - 1;
+          bal &= bal - 1;
+          const int r0 = w * CD_ROWS_PER_WARP + ln * CD_R;
+          for (int k = 0; k < CD_R; ++k) {
+            const double* q = s_rows + (r0 + k) * 3;
+            const double d = G::d(cx, cy, cz, q[0], q[1], q[2]);
+            // rows ascend in (warp, lane, k) order: strict '<' keeps the lowest
+            if (brow < 0 || d < bd) {
+              if (!(d != d)) {
+                bd = d;
+                brow = r0 + k;
+              }
+            }
+          }
+        }
+      }
+      if (brow >= 0)
+        key128_min(keys2 + b * M + tc + col, (u64)__double_as_longlong(bd), (u64)(blk_row0 + brow));
     }
   }
+  // rows: exact value and lowest column from the recorded chunk, or from the
+  // whole segment when a tie on the high word was seen
   if (warp_active) {
-#pragma unroll
-    for (int r = 0; r < CG_R; ++r) {
-      const int64_t row = lane_row0 + r;
-      if (row < row_end) KO::flush(keys1 + b * N + row, KO::make(best[r], (unsigned)bchunk[r]));
+    const double* seg_cols = xyz2 + b * M * 3;
+#pragma unroll 1
+    for (int r = 0; r < CD_R; ++r) {
+      const int64_t row = warp_row0 + (int64_t)lane * CD_R + r;
+      if (row >= row_end || mh[r] == 0xffffffffu) continue;
+      const bool tie = (ties >> r) & 1u;
+      const double* q = s_rows + (lrow0 + r) * 3;
+      const int64_t j0 = tie ? c0 : bchunk[r];
+      const int64_t j1 = tie ? c1 : min64(c1, (int64_t)bchunk[r] + CD_C);
+      double bd = 0.0;
+      int64_t bj = -1;
+      for (int64_t j = j0; j < j1; ++j) {
+        const double* c = seg_cols + j * 3;
+        const double d = G::d(__ldg(c), __ldg(c + 1), __ldg(c + 2), q[0], q[1], q[2]);
+        if (!(d != d) && (bj < 0 || d < bd)) {
+          bd = d;
+          bj = j;
+        }
+      }
+      if (bj >= 0) key128_min(keys1 + b * N + row, (u64)__double_as_longlong(bd), (u64)bj);
     }
   }
-  pdl_trigger();  // the next kernel may be scheduled (it waits for this grid)
+  pdl_trigger();
 }
 
 // ------------------------------- finalize -------------------------------
@@ -1043,20 +1059,19 @@ int launch_keys_f16(const __half* x1, const __half* x2, int64_t B, int64_t N, in
                     p.rb_count, p.cs_count, p.seg, (u64*)k1, (u64*)k2);
 }
 
-template <typename T, int MODE>
-int launch_keys_generic(const T* x1, const T* x2, int64_t B, int64_t N, int64_t M, int64_t rb0,
-                        int64_t rb1, void* k1, void* k2, cudaStream_t st) {
-  using K = typename KeyOps<typename GenDist<T, MODE>::V>::K;
-  auto kern = chamfer_keys_generic_kernel<T, MODE>;
+template <int MODE>
+int launch_keys_f64(const double* x1, const double* x2, int64_t B, int64_t N, int64_t M, int64_t rb0,
+                    int64_t rb1, void* k1, void* k2, cudaStream_t st) {
+  auto kern = chamfer_keys_f64_kernel<MODE>;
   static thread_local int slots_cache[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
   int& slots = slots_cache[dev & 63];
-  if (!slots) slots = slots_for(kern, CG_MAXW * 32);
-  const Plan p = make_plan(B, rb1 - rb0, M, CG_ROWS_PER_WARP, CG_MAXW, slots);
+  if (!slots) slots = slots_for(kern, CD_W * 32);
+  const Plan p = make_plan(B, rb1 - rb0, M, CD_ROWS_PER_WARP, CD_W, slots);
   if (p.ctas <= 0) return TPO_OK;
   return launch_pdl(kern, dim3((unsigned)p.ctas), dim3(p.warps * 32), 0, st, x1, x2, N, M, rb0, rb1,
-                    p.rb_count, p.cs_count, p.seg, (K*)k1, (K*)k2);
+                    p.rb_count, p.cs_count, p.seg, (Key128*)k1, (Key128*)k2);
 }
 
 template <typename T, int MODE, int ROWCH, int COLCH>
@@ -1092,8 +1107,8 @@ int chamfer_fwd_keys(int dtype, int flags, const void* x1, const void* x2, int64
     case TPO_F16:
       return launch_keys_f16((const __half*)x1, (const __half*)x2, B, N, M, rb0, rb1, k1, k2, st);
     case TPO_F64:
-      return exact ? launch_keys_generic<double, TPO_ROUND_EXACT>((const double*)x1, (const double*)x2, B, N, M, rb0, rb1, k1, k2, st)
-                   : launch_keys_generic<double, TPO_ROUND_FMA>((const double*)x1, (const double*)x2, B, N, M, rb0, rb1, k1, k2, st);
+      return exact ? launch_keys_f64<TPO_ROUND_EXACT>((const double*)x1, (const double*)x2, B, N, M, rb0, rb1, k1, k2, st)
+                   : launch_keys_f64<TPO_ROUND_FMA>((const double*)x1, (const double*)x2, B, N, M, rb0, rb1, k1, k2, st);
   }
   return TPO_ERR_INVALID_ARGUMENT;
 }

@@ -78,32 +78,21 @@ class KnnUnits:
     """One rank's share of a ragged knn batch, as (batch, query-row range) units
     balanced by lengths1*lengths2 work over the ranks (partition.knn_units).
 
-    The units are packed into one padded batch (S units, longest unit's rows) by
-    gathers whose index tensors are built once here, so the rank runs ONE
-    knn_points launch over all of its units; autograd carries the gradients back
-    through the gathers into the full (B, P, 3) inputs.  Indices returned by
-    the knn are indices into the unit's own batch of p2, as in the unsplit call."""
+    Each unit runs as its own knn_points call on views of the inputs (a unit's
+    query rows are one contiguous slice of a batch), so nothing is copied;
+    autograd accumulates the units' gradients into the full (B, P, D) inputs.
+    Indices returned by the knn are indices into the unit's batch of p2, as in
+    the unsplit call.  A rank holds at most a few units (cuts fall only where a
+    rank's share ends)."""
 
     def __init__(self, lengths1, lengths2, world: int, rank: int, device):
         l1 = [int(v) for v in lengths1]
         l2 = [int(v) for v in lengths2]
         self.units = knn_units(l1, l2, world, rank)
-        S = len(self.units)
-        L = max([r1 - r0 for _, r0, r1 in self.units], default=0)
-        b = torch.tensor([u[0] for u in self.units], dtype=torch.int64)
-        r0 = torch.tensor([u[1] for u in self.units], dtype=torch.int64)
-        n = torch.tensor([u[2] - u[1] for u in self.units], dtype=torch.int64)
-        rows = r0[:, None] + torch.arange(L, dtype=torch.int64)[None, :]
-        rows = torch.minimum(rows, (r0 + n - 1).clamp_min(0)[:, None])  # pad rows repeat the last valid one
-        self.batch = b.to(device)
-        self.rows = rows.to(device)
-        self.lengths1 = n.to(device)
-        self.lengths2 = torch.tensor([l2[u[0]] for u in self.units], dtype=torch.int64).to(device)
+        self.lengths1 = [torch.tensor([r1 - r0], dtype=torch.int64, device=device)
+                         for _, r0, r1 in self.units]
+        self.lengths2 = [torch.tensor([l2[b]], dtype=torch.int64, device=device) for b, _, _ in self.units]
         self.work = sum((r1 - r0) * l2[bb] for bb, r0, r1 in self.units)
-
-    def gather(self, p1, p2):
-        """(p1_units (S, L, D), p2_units (S, P2, D)), differentiable gathers."""
-        return p1[self.batch[:, None], self.rows], p2[self.batch]
 
 
 def sharded_knn_loss(p1, p2, units: KnnUnits, K: int, group=None, norm: int = 2,
@@ -119,12 +108,13 @@ def sharded_knn_loss(p1, p2, units: KnnUnits, K: int, group=None, norm: int = 2,
     a = p1.detach().requires_grad_()
     b = p2.detach().requires_grad_()
     if len(units.units):
-        pa, pb = units.gather(a, b)
-        idx, d = knn_points(pa, pb, units.lengths1, units.lengths2, norm=norm, K=K)
-        nn = knn_gather(pb, idx, units.lengths2)
-        # padded rows (beyond the unit's length) carry idx -1 / dist 0 and
-        # gather zero: they add nothing to the loss or the gradients
-        loss = d.sum() + nn.sum()
+        loss = None
+        for (bb, r0, r1), la, lb in zip(units.units, units.lengths1, units.lengths2):
+            pa, pb = a[bb:bb + 1, r0:r1], b[bb:bb + 1]
+            idx, d = knn_points(pa, pb, la, lb, norm=norm, K=K)
+            nn = knn_gather(pb, idx, lb)
+            part = d.sum() + nn.sum()
+            loss = part if loss is None else loss + part
         ga, gb = torch.autograd.grad(loss, [a, b])
         loss = loss.detach()
     else:
