@@ -450,17 +450,32 @@ __global__ void __launch_bounds__(KW * 32)
 #define TPO_KS 1
 #endif
 
+template <int Q>
+static int launch_knn_f32x3_q(const float* p1, const float* p2, const int64_t* l1, const int64_t* l2,
+                              int64_t N, int64_t P1, int64_t P2, int K, float* dists, int64_t* idxs,
+                              cudaStream_t st) {
+  const int qblocks = (int)((P1 + KW * Q - 1) / (KW * Q));
+  const int64_t ctas = N * qblocks;
+  if (ctas <= 0) return TPO_OK;
+  knn_fwd_f32x3_kernel<Q, TPO_KS><<<(unsigned)ctas, KW * 32, 0, st>>>(p1, p2, l1, l2, N, P1, P2, K,
+                                                                     qblocks, dists, idxs);
+  return check_launch();
+}
+
+// TPO_KQF queries per warp; 2 when that leaves fewer CTAs than about two per SM
+// (small problems, e.g. one rank's share of a split batch), so every SM has work.
 static int launch_knn_f32x3(const float* p1, const float* p2, const int64_t* l1, const int64_t* l2,
                             int64_t N, int64_t P1, int64_t P2, int K, float* dists, int64_t* idxs,
                             cudaStream_t st) {
   constexpr int Q = TPO_KQF;
-  constexpr int S = TPO_KS;
-  const int qblocks = (int)((P1 + KW * Q - 1) / (KW * Q));
-  const int64_t ctas = N * qblocks;
-  if (ctas <= 0) return TPO_OK;
-  knn_fwd_f32x3_kernel<Q, S><<<(unsigned)ctas, KW * 32, 0, st>>>(p1, p2, l1, l2, N, P1, P2, K, qblocks,
-                                                             dists, idxs);
-  return check_launch();
+  static int sms[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!sms[dev & 63]) cudaDeviceGetAttribute(&sms[dev & 63], cudaDevAttrMultiProcessorCount, dev);
+  const int64_t ctas = N * ((P1 + KW * Q - 1) / (KW * Q));
+  if (Q > 2 && ctas < 2LL * sms[dev & 63])
+    return launch_knn_f32x3_q<2>(p1, p2, l1, l2, N, P1, P2, K, dists, idxs, st);
+  return launch_knn_f32x3_q<Q>(p1, p2, l1, l2, N, P1, P2, K, dists, idxs, st);
 }
 
 template <typename T, int DT, int NORM, int MODE>

@@ -78,21 +78,44 @@ class KnnUnits:
     """One rank's share of a ragged knn batch, as (batch, query-row range) units
     balanced by lengths1*lengths2 work over the ranks (partition.knn_units).
 
-    Each unit runs as its own knn_points call on views of the inputs (a unit's
-    query rows are one contiguous slice of a batch), so nothing is copied;
-    autograd accumulates the units' gradients into the full (B, P, D) inputs.
-    Indices returned by the knn are indices into the unit's batch of p2, as in
-    the unsplit call.  A rank holds at most a few units (cuts fall only where a
-    rank's share ends)."""
+    The rank's units run as ONE packed knn launch: the units' query rows are
+    gathered into a (S, Lmax, D) batch and their target clouds into (S, P2, D)
+    (small copies, index tensors built once here), because a launch per unit
+    would leave most SMs idle (one batch of config 4 is ~200 CTAs).  Indices
+    returned by the knn are indices into the unit's batch of p2, as in the
+    unsplit call."""
 
     def __init__(self, lengths1, lengths2, world: int, rank: int, device):
         l1 = [int(v) for v in lengths1]
         l2 = [int(v) for v in lengths2]
         self.units = knn_units(l1, l2, world, rank)
-        self.lengths1 = [torch.tensor([r1 - r0], dtype=torch.int64, device=device)
-                         for _, r0, r1 in self.units]
-        self.lengths2 = [torch.tensor([l2[b]], dtype=torch.int64, device=device) for b, _, _ in self.units]
+        S = len(self.units)
+        L = max([r1 - r0 for _, r0, r1 in self.units], default=0)
+        self.L = L
+        b = torch.tensor([u[0] for u in self.units], dtype=torch.int64)
+        r0 = torch.tensor([u[1] for u in self.units], dtype=torch.int64)
+        n = torch.tensor([u[2] - u[1] for u in self.units], dtype=torch.int64)
+        k = torch.arange(L, dtype=torch.int64)[None, :]
+        rows = r0[:, None] + torch.minimum(k, (n - 1).clamp_min(0)[:, None])  # pads repeat a valid row
+        self.batch = b.to(device)
+        self._valid = (k < n[:, None]).reshape(-1)  # packed rows that are real (host)
+        self.lengths1 = n.to(device)
+        self.lengths2 = torch.tensor([l2[u[0]] for u in self.units], dtype=torch.int64).to(device)
         self.work = sum((r1 - r0) * l2[bb] for bb, r0, r1 in self.units)
+        self._rows = rows
+        self._b = b
+
+    def index(self, P1: int):
+        """Device index tensors for a (B*P1, D) view of p1, built on the host
+        once per P1: (flat row of every packed row, flat row of every real packed
+        row, packed position of every real packed row)."""
+        if getattr(self, "_P1", None) != P1:
+            flat = (self._b[:, None] * P1 + self._rows).reshape(-1)
+            pos = torch.nonzero(self._valid).reshape(-1)
+            dev = self.batch.device
+            self._idx = (flat.to(dev), flat[pos].to(dev), pos.to(dev))
+            self._P1 = P1
+        return self._idx
 
 
 def sharded_knn_loss(p1, p2, units: KnnUnits, K: int, group=None, norm: int = 2,
@@ -102,24 +125,31 @@ def sharded_knn_loss(p1, p2, units: KnnUnits, K: int, group=None, norm: int = 2,
     identical on every rank after one all_reduce(SUM) of the gradients (the
     rank's units write disjoint rows of grad_p1 but may share a batch's p2).
     reduce=False returns this rank's partial sums without the collective (for a
-    caller that captures the compute in a CUDA graph and reduces after it)."""
-    from .knn import knn_gather, knn_points
+    caller that captures the compute in a CUDA graph and reduces after it).
 
-    a = p1.detach().requires_grad_()
-    b = p2.detach().requires_grad_()
+    The gradients are formed with the library's own backward ops (the same the
+    autograd path calls): d loss/d dists = 1 and d loss/d nn = 1."""
+    ops = _lib.knn_ops
+    B, P1, D = p1.shape
+    P2 = p2.shape[1]
+    ga = torch.zeros_like(p1)
+    gb = torch.zeros_like(p2)
     if len(units.units):
-        loss = None
-        for (bb, r0, r1), la, lb in zip(units.units, units.lengths1, units.lengths2):
-            pa, pb = a[bb:bb + 1, r0:r1], b[bb:bb + 1]
-            idx, d = knn_points(pa, pb, la, lb, norm=norm, K=K)
-            nn = knn_gather(pb, idx, lb)
-            part = d.sum() + nn.sum()
-            loss = part if loss is None else loss + part
-        ga, gb = torch.autograd.grad(loss, [a, b])
-        loss = loss.detach()
+        flat, dst, src = units.index(P1)
+        S, L = len(units.units), units.L
+        pa = p1.reshape(B * P1, D).index_select(0, flat).view(S, L, D)
+        pb = p2.index_select(0, units.batch)
+        idx, d = ops.knn_forward(pa, pb, units.lengths1, units.lengths2, norm, K, -1)
+        nn = ops.knn_gather_forward(pb, idx, units.lengths2)
+        loss = d.sum() + nn.sum()
+        g1, g2 = ops.knn_backward(pa, pb, units.lengths1, units.lengths2, idx, norm, torch.ones_like(d))
+        g2 = g2 + ops.knn_gather_backward(torch.ones_like(nn), idx, units.lengths2, P2)
+        # packed rows back to their places: real rows are disjoint; p2 grads of
+        # units sharing a batch add up
+        ga.view(B * P1, D).index_copy_(0, dst, g1.reshape(S * L, D).index_select(0, src))
+        gb.index_add_(0, units.batch, g2)
     else:
         loss = torch.zeros((), dtype=p1.dtype, device=p1.device)
-        ga, gb = torch.zeros_like(p1), torch.zeros_like(p2)
     if reduce and dist.is_initialized() and dist.get_world_size(group) > 1:
         flat = torch.cat([ga.reshape(-1), gb.reshape(-1), loss.reshape(1)])
         dist.all_reduce(flat, group=group)
