@@ -882,8 +882,16 @@ def knn_roofline(cfg, inputs, dev, clocks, reps=20):
 # configuration's dominant kernel, from an ncu capture of this build on a B200,
 # with how it was taken.  Configurations without a capture report null.
 TRAFFIC = {
-    CONFIGS["4"]["desc"]: (1109248, "ncu capture of knn_fwd_kernel, config 4 (one launch)"),
+    CONFIGS["4"]["desc"]: (1117184, "ncu capture of knn_fwd_f32x3_kernel, config 4 (one launch)"),
     CONFIGS["2"]["desc"]: (2686976, "ncu capture of chamfer_keys_f32_kernel, config 2 (one launch)"),
+    CONFIGS["5s"]["desc"]: (5308416, "ncu capture of chamfer_keys_f32_kernel, config 5 scene at 2^17"),
+    CONFIGS["5sd"]["desc"]: (12062208, "ncu capture of chamfer_keys_f64_kernel, config 5 scene at 2^17"),
+    # both 2^20 clouds stay L2-resident, so DRAM traffic grows with the cloud
+    # size (8x the 2^17 capture), not with the pairs
+    CONFIGS["5"]["desc"]: (8 * 5308416, "8x the 2^17 capture of chamfer_keys_f32_kernel (clouds "
+                                        "L2-resident: traffic scales with cloud size)"),
+    CONFIGS["5d"]["desc"]: (8 * 12062208, "8x the 2^17 capture of chamfer_keys_f64_kernel (clouds "
+                                          "L2-resident: traffic scales with cloud size)"),
 }
 
 
