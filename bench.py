@@ -268,10 +268,11 @@ def launches_per_step(cfg, mode="single"):
     return {"chamfer": 4, "knn": 4, "fps": 1}[cfg["kind"]]
 
 
-def parity_rows(dev, ws):
+def parity_rows(dev, ws, dtype=torch.float32):
     """Row-sharded vs single-GPU on a 2^16-point LiDAR-like scene, on every rank:
-    loss within 1e-6 relative, gradients within twice the per-element fp32 bound
-    (1e-6 of the summed term magnitudes; both sides sum in a free order)."""
+    loss within the dtype's relative tolerance (1e-6 fp32, 1e-12 fp64), gradients
+    within twice the per-element bound of tests/tolerances.py (both sides sum in
+    a free order)."""
     import numpy as np
 
     import datagen
@@ -279,22 +280,23 @@ def parity_rows(dev, ws):
     from tolerances import term_scale, tolerance
     from torch_point_ops_b200.sharded import sharded_chamfer_loss
 
-    x1 = datagen.lidar(1 << 16, seed=77).to(dev)
-    x2 = datagen.lidar(1 << 16, seed=78).to(dev)
+    x1 = datagen.lidar(1 << 16, seed=77, dtype=dtype).to(dev)
+    x2 = datagen.lidar(1 << 16, seed=78, dtype=dtype).to(dev)
     loss, g1, g2 = sharded_chamfer_loss(x1, x2)
     a, b = x1.clone().requires_grad_(), x2.clone().requires_grad_()
     ref = tpo.ChamferDistance("mean")(a, b)
     ra, rb = torch.autograd.grad(ref, [a, b])
     _, _, i1, i2 = tpo.chamfer_distance_with_idx(x1, x2)
     n = x1.shape[1]
-    gg = torch.full((1, n), 1.0 / n)
+    gg = torch.full((1, n), 1.0 / n, dtype=dtype)
     s1, s2, n1, n2 = term_scale(x1.cpu(), x2.cpu(), i1.cpu(), i2.cpu(), gg, gg)
     e1 = np.abs(g1.cpu().double().numpy() - ra.cpu().double().numpy())
     e2 = np.abs(g2.cpu().double().numpy() - rb.cpu().double().numpy())
     lerr = abs(float(loss) - float(ref)) / abs(float(ref))
-    ok = (lerr <= 1e-6 and bool(np.all(e1 <= 2 * tolerance(torch.float32, s1, n1)))
-          and bool(np.all(e2 <= 2 * tolerance(torch.float32, s2, n2))))
-    return ok, {"scene": "2^16 x 2^16 LiDAR-like, fp32", "loss_rel_err": lerr,
+    rel = {torch.float32: 1e-6, torch.float64: 1e-12}[dtype]
+    ok = (lerr <= rel and bool(np.all(e1 <= 2 * tolerance(dtype, s1, n1)))
+          and bool(np.all(e2 <= 2 * tolerance(dtype, s2, n2))))
+    return ok, {"scene": f"2^16 x 2^16 LiDAR-like, {str(dtype).replace('torch.', '')}", "loss_rel_err": lerr,
                 "grad_max_abs_err": float(max(e1.max(), e2.max()))}
 
 
@@ -377,7 +379,7 @@ def run_ours(args, cfg):
 
     parity = None
     if mode == "rows":
-        ok, info = parity_rows(dev, ws)
+        ok, info = parity_rows(dev, ws, getattr(torch, cfg["dtype"]))
     elif mode == "strong":
         ok, info = parity_strong(cfg, step, glob_inputs, diff, dev)
     if mode != "single":
