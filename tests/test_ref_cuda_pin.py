@@ -164,3 +164,45 @@ def test_reference_knn_cuda_f16(ragged):
         rr = ((dx * dx).half().float() + (dy * dy).half().float()).half().float()
         rr = (rr + (dz * dz).half().float()).half()
         assert np.array_equal(_bits(rr), _bits(rdb))
+
+
+@pytest.mark.parametrize("cfg", ["2", "2h", "3"])
+def test_reference_chamfer_cuda_full_size(cfg):
+    """Benchmark configurations 2 (fp32, fp16) and 3 at full size: indices and
+    distances bit-identical to the reference CUDA kernel's, every point."""
+    ops = oracle.ref_chamfer()
+    if ops is None:
+        pytest.skip("reference CUDA build not present in oracle/_ref")
+    if cfg == "3":
+        x1, x2 = datagen.gmm(16, 16384, seed=30), datagen.gmm(16, 8192, seed=31)
+    else:
+        dt = torch.float16 if cfg == "2h" else torch.float32
+        x1, x2 = datagen.sphere_noise(32, 2048, seed=20, dtype=dt), datagen.sphere_noise(32, 2048, seed=21, dtype=dt)
+    rd1, rd2, ri1, ri2 = ops.chamfer_forward(x1.cuda(), x2.cuda())
+    d1, d2, i1, i2 = C.chamfer_fwd(x1.cuda(), x2.cuda(), 0)
+    assert torch.equal(i1.cpu(), ri1.cpu()) and torch.equal(i2.cpu(), ri2.cpu())
+    assert np.array_equal(_bits(d1), _bits(rd1)) and np.array_equal(_bits(d2), _bits(rd2))
+
+
+def test_reference_knn_cuda_config4_full_size():
+    """Benchmark configuration 4 at full size (K=16, ragged lengths): the valid
+    entries of every valid row equal the reference CUDA kernel's after its own
+    python sort -- distances bit for bit, indices wherever the distance is not
+    tied within the row's K (the reference orders equal distances freely)."""
+    ops = oracle.ref_knn()
+    if ops is None or not oracle._ref_loaded.get("knn_cuda_ref.so"):
+        pytest.skip("reference CUDA knn build not present in oracle/_ref")
+    p1, p2, l1, l2 = [t.cuda() for t in datagen.knn_config4(seed=4)]
+    K = 16
+    ri, rd = ops.knn_forward(p1, p2, l1, l2, 2, K, -1)
+    rd, order = rd.sort(dim=2)
+    ri = ri.gather(2, order)
+    i, d = C.knn_fwd(p1, p2, l1, l2, 2, K, 0)
+    for b in range(p1.shape[0]):
+        L1 = int(l1[b])
+        db, rdb = d[b, :L1].cpu(), rd[b, :L1].cpu()
+        assert np.array_equal(_bits(db), _bits(rdb))
+        dv = db.numpy()
+        uniq = np.sum(dv[:, :, None] == dv[:, None, :], axis=2) == 1
+        assert np.array_equal(i[b, :L1].cpu().numpy()[uniq], ri[b, :L1].cpu().numpy()[uniq])
+        assert uniq.mean() > 0.999
