@@ -275,9 +275,13 @@ static __device__ unsigned g_knn_device_error = 0;
 #define TPO_KT3 1024
 #endif
 constexpr int KT3 = TPO_KT3;  // targets per tile (two tiles in shared memory)
+#ifndef TPO_KW3
+#define TPO_KW3 8
+#endif
+constexpr int KW3 = TPO_KW3;  // warps per CTA of the fp32 D=3 kernel
 
 template <int KQF, int KS>
-__global__ void __launch_bounds__(KW * 32)
+__global__ void __launch_bounds__(KW3 * 32)
     knn_fwd_f32x3_kernel(const float* __restrict__ p1, const float* __restrict__ p2,
                          const int64_t* __restrict__ len1, const int64_t* __restrict__ len2,
                          int64_t N, int64_t P1, int64_t P2, int K, int qblocks,
@@ -288,7 +292,7 @@ __global__ void __launch_bounds__(KW * 32)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int64_t n = blockIdx.x / qblocks;
-  const int64_t blk_q0 = (int64_t)(blockIdx.x % qblocks) * (KW * KQF);
+  const int64_t blk_q0 = (int64_t)(blockIdx.x % qblocks) * (KW3 * KQF);
   const int64_t q0 = blk_q0 + warp * KQF;
   const int64_t L1 = len1 ? min64(max64(len1[n], 0), P1) : P1;
   const int64_t L2 = len2 ? min64(max64(len2[n], 0), P2) : P2;
@@ -391,16 +395,17 @@ __global__ void __launch_bounds__(KW * 32)
 #pragma unroll
           for (int st = 0; st < KS; ++st) {
             const int cbase = (int)t0 + (bt * KS + st) * KSTEP;
-            unsigned bals[KQF];  // all ballots first: independent, issued back to back
+            // this lane's pass bits (one per query, from the sign bits) and,
+            // by one redux, the warp's set of queries with candidates
+            unsigned m = 0;
+#pragma unroll
+            for (int ip = 0; ip < KQF / 2; ++ip)
+              m |= (((unsigned)sg[st][ip] >> 31) | (((unsigned)(sg[st][ip] >> 32) >> 31) << 1)) << (2 * ip);
+            const unsigned qm = __reduce_or_sync(0xffffffffu, m);
 #pragma unroll
             for (int i = 0; i < KQF; ++i) {
-              const unsigned w = (i & 1) ? (unsigned)(sg[st][i >> 1] >> 32) : (unsigned)sg[st][i >> 1];
-              bals[i] = __ballot_sync(0xffffffffu, (int)w < 0);
-            }
-#pragma unroll
-            for (int i = 0; i < KQF; ++i) {
-              unsigned bal = bals[i];
-              bool changed = false;
+              if (!((qm >> i) & 1u)) continue;
+              unsigned bal = __ballot_sync(0xffffffffu, (m >> i) & 1u);
               while (bal) {
                 const int src = __ffs(bal) - 1;
                 bal &= bal - 1;
@@ -416,12 +421,9 @@ __global__ void __launch_bounds__(KW * 32)
                   Ld[i] = take_prev ? upd : cd;
                   Li[i] = take_prev ? upi : cbase + src;
                 }
-                changed = true;
               }
-              if (changed) {
-                thr[i] = __shfl_sync(0xffffffffu, Ld[i], K - 1);
-                THR[i >> 1] = pk(thr[i & ~1], thr[i | 1]);
-              }
+              thr[i] = __shfl_sync(0xffffffffu, Ld[i], K - 1);
+              THR[i >> 1] = pk(thr[i & ~1], thr[i | 1]);
             }
           }
         }
@@ -454,10 +456,10 @@ template <int Q>
 static int launch_knn_f32x3_q(const float* p1, const float* p2, const int64_t* l1, const int64_t* l2,
                               int64_t N, int64_t P1, int64_t P2, int K, float* dists, int64_t* idxs,
                               cudaStream_t st) {
-  const int qblocks = (int)((P1 + KW * Q - 1) / (KW * Q));
+  const int qblocks = (int)((P1 + KW3 * Q - 1) / (KW3 * Q));
   const int64_t ctas = N * qblocks;
   if (ctas <= 0) return TPO_OK;
-  knn_fwd_f32x3_kernel<Q, TPO_KS><<<(unsigned)ctas, KW * 32, 0, st>>>(p1, p2, l1, l2, N, P1, P2, K,
+  knn_fwd_f32x3_kernel<Q, TPO_KS><<<(unsigned)ctas, KW3 * 32, 0, st>>>(p1, p2, l1, l2, N, P1, P2, K,
                                                                      qblocks, dists, idxs);
   return check_launch();
 }
@@ -472,7 +474,7 @@ static int launch_knn_f32x3(const float* p1, const float* p2, const int64_t* l1,
   int dev = 0;
   cudaGetDevice(&dev);
   if (!sms[dev & 63]) cudaDeviceGetAttribute(&sms[dev & 63], cudaDevAttrMultiProcessorCount, dev);
-  const int64_t ctas = N * ((P1 + KW * Q - 1) / (KW * Q));
+  const int64_t ctas = N * ((P1 + KW3 * Q - 1) / (KW3 * Q));
   if (Q > 2 && ctas < 2LL * sms[dev & 63])
     return launch_knn_f32x3_q<2>(p1, p2, l1, l2, N, P1, P2, K, dists, idxs, st);
   return launch_knn_f32x3_q<Q>(p1, p2, l1, l2, N, P1, P2, K, dists, idxs, st);
