@@ -78,3 +78,33 @@ def test_sharded_matches_single(world, dtype):
         p.join(timeout=300)
         assert p.exitcode == 0
     assert q.get(timeout=10)
+
+
+@pytest.mark.parametrize("world", [1, 3, 8])
+def test_knn_units_sum_to_whole_batch_on_one_gpu(world):
+    """The ragged-knn split (partition.knn_units + sharded_knn_loss): the ranks'
+    partial losses and gradients, computed one after another on one GPU with no
+    collective and summed here, equal the whole batch through the public API
+    (distances feed the loss bit-exactly; gradients are sums in a free order)."""
+    import torch_point_ops_b200 as tpo
+    from torch_point_ops_b200.sharded import KnnUnits, sharded_knn_loss
+
+    p1, p2, l1, l2 = datagen.knn_config4(seed=12, B=4, P=1024)
+    dev = "cuda"
+    a = p1.to(dev).requires_grad_()
+    b = p2.to(dev).requires_grad_()
+    _, d, nn = tpo.KNearestNeighbors(K=8, return_nn=True)(a, b, l1.to(dev), l2.to(dev))
+    ref = d.sum() + nn.sum()
+    ga, gb = torch.autograd.grad(ref, [a, b])
+    loss = 0.0
+    g1 = torch.zeros_like(ga)
+    g2 = torch.zeros_like(gb)
+    for r in range(world):
+        units = KnnUnits(l1, l2, world, r, dev)
+        lo, x, y = sharded_knn_loss(p1.to(dev), p2.to(dev), units, 8, reduce=False)
+        loss += float(lo)
+        g1 += x
+        g2 += y
+    assert abs(loss - float(ref)) <= 1e-5 * abs(float(ref))
+    torch.testing.assert_close(g1, ga, rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(g2, gb, rtol=1e-5, atol=1e-5)
