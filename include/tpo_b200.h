@@ -183,7 +183,7 @@ TPO_API int tpo_chamfer_loss_bwd_workspace(int dtype, int flags, const void* xyz
  * For each valid query (p < lengths1[n]) the K smallest (dist, idx) pairs over
  * the first lengths2[n] points, ascending by (dist, idx).  Slots k >= lengths2[n]
  * and rows p >= lengths1[n] hold idx -1 / dist 0 (the reference CPU padding,
- * knn.cpp:44-45).  norm: 2 = squared L2, 1 = L1.  1 <= K <= 256 (larger K returns
+ * knn.cpp:44-45).  norm: 2 = squared L2, 1 = L1.  1 <= K <= 1024 (larger K returns
  * TPO_ERR_UNSUPPORTED), any D >= 1; D <= 8 with K <= 32 takes the fast kernel. */
 TPO_API int tpo_knn_fwd(int dtype, int flags, const void* p1, const void* p2,
                 const int64_t* lengths1, const int64_t* lengths2, int64_t N, int64_t P1,

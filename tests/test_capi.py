@@ -48,7 +48,7 @@ def test_knn_argument_checks():
                                I64(norm), I64(K), VP(1), VP(1), VP(0))
     assert L.tpo_knn_fwd(*args(3, 1, 3)) == 1          # bad norm
     assert L.tpo_knn_fwd(*args(2, 0, 3)) == 1          # K < 1
-    assert L.tpo_knn_fwd(*args(2, 257, 3)) == 2        # K > 256: unsupported
+    assert L.tpo_knn_fwd(*args(2, 1025, 3)) == 2       # K > 1024: unsupported
     assert L.tpo_knn_fwd(*args(2, 4, 0)) == 1          # D < 1
 
 

@@ -77,11 +77,12 @@ def test_knn_general_d(D):
 
 
 @pytest.mark.parametrize("D,K", [(9, 5), (16, 32), (32, 7), (64, 3), (3, 33), (3, 64),
-                                 (12, 100), (2, 256)])
+                                 (12, 100), (2, 256), (3, 300), (4, 700), (3, 1024)])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float64, torch.float16])
 def test_knn_large_d_and_k(D, K, dtype):
-    """The general kernel: any D (the reference's V0/V1 range) and K up to 256."""
-    p1, p2, l1, l2 = _case(2, 70, 300, D, dtype, seed=D * 100 + K)
+    """The general kernel: any D (the reference's V0/V1 range) and K up to 1024
+    (K beyond a batch's target count pads with idx -1)."""
+    p1, p2, l1, l2 = _case(2, 70, 1200 if K > 256 else 300, D, dtype, seed=D * 100 + K)
     _run(p1, p2, l1, l2, 2, K)
     _run(p1, p2, l1, l2, 1, K)
 
@@ -98,10 +99,10 @@ def test_knn_k_limit():
 
     x = torch.zeros(1, 4, 3, device=DEV)
     L = torch.full((1,), 4, device=DEV)
-    d = torch.empty(1, 4, 257, device=DEV)
-    i = torch.empty(1, 4, 257, dtype=torch.int64, device=DEV)
+    d = torch.empty(1, 4, 1025, device=DEV)
+    i = torch.empty(1, 4, 1025, dtype=torch.int64, device=DEV)
     rc = C.lib().tpo_knn_fwd(0, 0, C.p(x), C.p(x), C.p(L), C.p(L), C.I64(1), C.I64(4), C.I64(4),
-                             C.I64(3), C.I64(2), C.I64(257), C.p(d), C.p(i), C.stream())
+                             C.I64(3), C.I64(2), C.I64(1025), C.p(d), C.p(i), C.stream())
     assert rc == 2  # TPO_ERR_UNSUPPORTED
 
 

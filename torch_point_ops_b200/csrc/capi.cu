@@ -305,7 +305,7 @@ static int check_knn(int dtype, const void* p1, const void* p2, int64_t N, int64
   if (N < 0 || P1 < 0 || P2 < 0 || D < 1) return fail(TPO_ERR_INVALID_ARGUMENT, "knn: bad shape");
   if (norm != 1 && norm != 2) return fail(TPO_ERR_INVALID_ARGUMENT, "Norm must be 1 or 2.");
   if (K < 1) return fail(TPO_ERR_INVALID_ARGUMENT, "knn: K must be >= 1");
-  if (K > kKnnMaxK) return fail(TPO_ERR_UNSUPPORTED, "knn: this build supports K <= 256");
+  if (K > kKnnMaxK) return fail(TPO_ERR_UNSUPPORTED, "knn: this build supports K <= 1024");
   if (P2 >= (int64_t(1) << 31)) return fail(TPO_ERR_INVALID_ARGUMENT, "knn: P2 limited to 2^31-1");
   if ((N * P1 > 0 && !p1) || (N * P2 > 0 && !p2)) return fail(TPO_ERR_INVALID_ARGUMENT, "knn: null input");
   return TPO_OK;

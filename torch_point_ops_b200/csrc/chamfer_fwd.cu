@@ -48,7 +48,10 @@ constexpr int CF_SUNROLL = TPO_CF_SUNROLL;
 constexpr int CF_R = TPO_CF_R;        // rows per lane
 constexpr int CF_RP = CF_R / 2;       // packed row pairs per lane
 constexpr int CF_C = 4;               // columns per sub-step
-constexpr int CF_CHUNK = 2 * CF_C;    // fp32 row-side chunk (columns per key)
+#ifndef TPO_CF_HS
+#define TPO_CF_HS 2
+#endif
+constexpr int CF_CHUNK = TPO_CF_HS * CF_C;  // fp32 row-side chunk (columns per key)
 constexpr int CF_HS = CF_CHUNK / CF_C;  // sub-steps per chunk
 constexpr int CH_CHUNK = 2 * CF_C;      // fp16 row-side chunk
 constexpr int CF_TILE_STEPS = 64;     // steps per shared-memory tile

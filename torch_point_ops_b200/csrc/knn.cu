@@ -632,7 +632,9 @@ static int dispatch_knn_general(const void* p1, const void* p2, const int64_t* l
   if (K <= 32) return launch_knn_general<T, NORM, 1>(p1, p2, l1, l2, N, P1, P2, D, K, dists, idxs, st);
   if (K <= 64) return launch_knn_general<T, NORM, 2>(p1, p2, l1, l2, N, P1, P2, D, K, dists, idxs, st);
   if (K <= 128) return launch_knn_general<T, NORM, 4>(p1, p2, l1, l2, N, P1, P2, D, K, dists, idxs, st);
-  return launch_knn_general<T, NORM, 8>(p1, p2, l1, l2, N, P1, P2, D, K, dists, idxs, st);
+  if (K <= 256) return launch_knn_general<T, NORM, 8>(p1, p2, l1, l2, N, P1, P2, D, K, dists, idxs, st);
+  if (K <= 512) return launch_knn_general<T, NORM, 16>(p1, p2, l1, l2, N, P1, P2, D, K, dists, idxs, st);
+  return launch_knn_general<T, NORM, 32>(p1, p2, l1, l2, N, P1, P2, D, K, dists, idxs, st);
 }
 
 template <typename T>

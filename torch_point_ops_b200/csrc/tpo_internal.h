@@ -35,7 +35,7 @@ int chamfer_bwd_accumulate(int dtype, const void* x1, const void* x2, int64_t B,
                            const void* gscalar, int scalar_mode, void* gx1, void* gx2,
                            cudaStream_t st);
 // Largest K of knn_forward (the list lives in registers, 8 rows of 32 lanes).
-constexpr int64_t kKnnMaxK = 256;
+constexpr int64_t kKnnMaxK = 1024;
 int knn_forward(int dtype, int flags, const void* p1, const void* p2, const int64_t* l1,
                 const int64_t* l2, int64_t N, int64_t P1, int64_t P2, int64_t D, int64_t norm,
                 int64_t K, void* dists, int64_t* idxs, cudaStream_t st);
