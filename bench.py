@@ -300,7 +300,7 @@ def parity_rows(dev, ws, dtype=torch.float32):
                 "grad_max_abs_err": float(max(e1.max(), e2.max()))}
 
 
-def parity_strong(cfg, step, glob_inputs, mine, dev):
+def parity_strong(cfg, step, glob_inputs, mine, dev, b_range=None):
     """--split strong vs the whole problem on one GPU (run on every rank):
     chamfer -- the global loss within 1e-6 relative and this rank's batches'
     gradients within the free-order summation bound; knn -- the global loss within
@@ -322,7 +322,7 @@ def parity_strong(cfg, step, glob_inputs, mine, dev):
 
         import torch_point_ops_b200 as tpo
         from tolerances import term_scale, tolerance
-        b0, b1 = mine[0].b_range
+        b0, b1 = b_range
         x1, x2 = mine[0].detach(), mine[1].detach()
         _, _, i1, i2 = tpo.chamfer_distance_with_idx(x1, x2)
         B = cfg["B"]
@@ -372,8 +372,6 @@ def run_ours(args, cfg):
         from torch_point_ops_b200.sharded import KnnUnits
         units = KnnUnits(host_inputs[2], host_inputs[3], ws, rank, dev)
     diff = [t.requires_grad_() if t.is_floating_point() and cfg["kind"] != "fps" else t for t in inputs]
-    if mode == "strong" and cfg["kind"] == "chamfer":
-        diff[0].b_range = (b0, b1)
     step, post = step_fn(cfg, mode, units=units, batch_share=share)
     flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)  # 256 MiB > L2
 
@@ -381,7 +379,8 @@ def run_ours(args, cfg):
     if mode == "rows":
         ok, info = parity_rows(dev, ws, getattr(torch, cfg["dtype"]))
     elif mode == "strong":
-        ok, info = parity_strong(cfg, step, glob_inputs, diff, dev)
+        ok, info = parity_strong(cfg, step, glob_inputs, diff, dev,
+                                 b_range=(b0, b1) if cfg["kind"] == "chamfer" else None)
     if mode != "single":
         t = torch.tensor([1 if ok else 0], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MIN)
