@@ -748,7 +748,7 @@ def pipe_peak(kind):
     """Measured whole-GPU rate of one arithmetic instruction kind on this device,
     in element results per second, and the SM clock it ran at (MHz), from the
     library's pipe probe (tpo_probe_pipe_peak: 8 independent fma chains per thread,
-    32 warps per SM, best of 3 launches).  kind: 0 fma.f32, 1 fma.f32x2,
+    32 warps per SM, best of 7 launches).  kind: 0 fma.f32, 1 fma.f32x2,
     2 fma.f16x2, 3 fma.f64."""
     if kind not in _PIPE_PEAKS:
         import ctypes

@@ -125,7 +125,7 @@ int pipe_probe(int kind, double* lane_ops_per_s, double* sm_mhz) {
   const int blocks = sms * 4, threads = 256;
   float best_ms = 1e30f;
   unsigned long long hclk[2] = {0, 1};
-  for (int rep = 0; rep < 4 && !s; ++rep) {  // rep 0 warms the clocks up
+  for (int rep = 0; rep < 8 && !s; ++rep) {  // rep 0 warms the clocks up
     kernels[kind]<<<blocks, threads, 0, st>>>(1.0f, sink, clk);
     s = check_launch();
     if (!s) s = cuda_status(cudaEventRecord(e0, st));
