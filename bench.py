@@ -838,8 +838,10 @@ KNN_INSTR_PER_PAIR = 8  # (dx*dx + dy*dy) + dz*dz, every operation rounded: 3 su
 
 
 def knn_roofline(cfg, inputs, dev, clocks, reps=20):
-    """The knn forward kernel alone (the knn_forward op: one launch) against the
-    FP32 pipe: valid pairs (sum of lengths1 * lengths2) over its device time.
+    """The knn forward op alone against the FP32 pipe: valid pairs (sum of
+    lengths1 * lengths2) over the device time of the whole op -- for fp32 D=3
+    that is three launches (knn_cells_kernel, knn_seed_kernel and the scan
+    knn_fwd_f32x3_kernel), all inside the timed region.
     The knn distance is the reference's exactly rounded ((dx*dx + dy*dy) + dz*dz),
     8 FP32-pipe operations per pair (no FMA), so the roofline is
     148 SM x 128 lanes x clock / 8."""
@@ -864,7 +866,7 @@ def knn_roofline(cfg, inputs, dev, clocks, reps=20):
     pairs = int((l1.long() * l2.long()).sum())
     achieved = pairs / (ms * 1e-3) / 1e9
     peak, basis = fp_peak_pairs(KNN_INSTR_PER_PAIR, (0,), 128)
-    out = {"bound": "fp32", "kernel": "knn_fwd_kernel", "achieved": round(achieved, 1),
+    out = {"bound": "fp32", "kernel": "knn_forward op (cells + seed + knn_fwd_f32x3_kernel)", "achieved": round(achieved, 1),
            "peak": round(peak, 1), "unit": "Gpair/s", "frac": round(achieved / peak, 4),
            **basis, "frac_of_nominal": round(achieved / basis["peak_nominal"], 4),
            "kernel_ms": round(ms, 4), "pairs_per_launch": pairs}
@@ -883,7 +885,8 @@ def knn_roofline(cfg, inputs, dev, clocks, reps=20):
 # configuration's dominant kernel, from an ncu capture of this build on a B200,
 # with how it was taken.  Configurations without a capture report null.
 TRAFFIC = {
-    CONFIGS["4"]["desc"]: (1117184, "ncu capture of knn_fwd_f32x3_kernel, config 4 (one launch)"),
+    CONFIGS["4"]["desc"]: (4355328, "ncu capture of knn_fwd_f32x3_kernel, config 4 (one launch; "
+                                    "cold caches, so the seeds in dists[:, :, 0] come from DRAM)"),
     CONFIGS["2"]["desc"]: (2686976, "ncu capture of chamfer_keys_f32_kernel, config 2 (one launch)"),
     CONFIGS["5s"]["desc"]: (5308416, "ncu capture of chamfer_keys_f32_kernel, config 5 scene at 2^17"),
     CONFIGS["5sd"]["desc"]: (12062208, "ncu capture of chamfer_keys_f64_kernel, config 5 scene at 2^17"),

@@ -18,6 +18,7 @@
 // Backward replaces KNearestNeighborBackwardKernel (knn.cu:401-466): one thread
 // per query row sums its K terms in k order (deterministic, no atomics for
 // grad_p1) and scatters the negated terms into grad_p2 with atomics.
+#include <cstdlib>
 #include <type_traits>
 
 #include "tpo_internal.h"
@@ -259,35 +260,53 @@ __global__ void __launch_bounds__(KW * 32)
 // fp32, D=3, squared L2 (the benchmark's knn case): the same warp-distributed
 // top-K lists, with the per-target work cut to the arithmetic plus one packed
 // op of filtering:
-//   * target tiles land by 1-D bulk copies (TMA) into two shared buffers: the
-//     copy of tile t+1 runs while tile t is scanned, so no warp waits on a load;
-//     a lane reads its target's x,y,z and forms the {c,c} pairs in registers;
-//   * the filter is ONE packed subtraction per query pair, d - thr: for floats
+//   * target tiles land by 1-D bulk copies (TMA) into two shared buffers (the
+//     copy of tile t+2 runs while tile t is scanned) and are rewritten once per
+//     tile into one structure-of-arrays tile, NaN padded to whole steps;
+//   * a step covers 64 targets, two per lane: one 64-bit shared load gives the
+//     lane's {x_a, x_b} (likewise y, z), and every query is held as {q, q}, so
+//     each packed fp32x2 sub/mul serves the lane's two targets; the adds are
+//     scalar .rn (the reference's ((dx*dx + dy*dy) + dz*dz), every operation
+//     rounded, never fused);
+//   * the filter is ONE packed subtraction per query, d - thr: for floats
 //     fl(d - thr) is negative exactly when d < thr (distinct floats never
 //     subtract to zero), +inf thresholds pass everything, the -inf threshold of
 //     an invalid query slot and the NaN padding pass nothing -- so the pass
-//     bits are sign bits, OR-ed across queries with logic ops;
-//   * KS steps share one warp vote; only then do the per-query ballots and
-//     insertions run (in step order, each candidate re-checked against the
-//     current threshold, so candidates still arrive in increasing index order).
+//     bits are sign bits, OR-ed across queries with logic ops, and one warp
+//     vote per step decides whether any insertion runs;
+//   * insertions run per query in increasing target index (lane-major, the
+//     lane's first target before its second), which with "land after equal
+//     entries" keeps the list "K smallest by (dist, idx)"; a candidate that
+//     passed a stale threshold lands at a lane >= K and never reaches the output.
+// SEED: the threshold starts at an upper bound of the query's K-th distance
+// (knn_seed_kernel below) instead of +inf.
 static __device__ unsigned g_knn_device_error = 0;
-#ifndef TPO_KT3
-#define TPO_KT3 1024
-#endif
-constexpr int KT3 = TPO_KT3;  // targets per tile (two tiles in shared memory)
+constexpr int KT3 = 1024;  // targets per tile (two bulk-copy buffers + one scan tile)
+constexpr int KP3 = 64;    // targets per step (two per lane)
 #ifndef TPO_KW3
 #define TPO_KW3 8
 #endif
 constexpr int KW3 = TPO_KW3;  // warps per CTA of the fp32 D=3 kernel
 
-template <int KQF, int KS>
+__device__ __forceinline__ void knn_list_insert(float& L, int& I, float cd, int ci, int lane) {
+  const float upd = __shfl_up_sync(0xffffffffu, L, 1);
+  const int upi = __shfl_up_sync(0xffffffffu, I, 1);
+  if (cd < L) {
+    const bool take_prev = lane > 0 && cd < upd;
+    L = take_prev ? upd : cd;
+    I = take_prev ? upi : ci;
+  }
+}
+
+template <int KQF, bool SEED>
 __global__ void __launch_bounds__(KW3 * 32)
     knn_fwd_f32x3_kernel(const float* __restrict__ p1, const float* __restrict__ p2,
                          const int64_t* __restrict__ len1, const int64_t* __restrict__ len2,
                          int64_t N, int64_t P1, int64_t P2, int K, int qblocks,
                          float* __restrict__ dists, int64_t* __restrict__ idxs) {
-  static_assert(KT3 % (KSTEP * KS) == 0 && KQF % 2 == 0, "tile/step shape");
+  static_assert(KT3 % KP3 == 0, "tile/step shape");
   __shared__ __align__(16) float s_raw[2][KT3 * 3];
+  __shared__ __align__(16) float s_soa[3][KT3];
   __shared__ __align__(8) unsigned long long s_bar[2];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -297,6 +316,7 @@ __global__ void __launch_bounds__(KW3 * 32)
   const int64_t L1 = len1 ? min64(max64(len1[n], 0), P1) : P1;
   const int64_t L2 = len2 ? min64(max64(len2[n], 0), P2) : P2;
   const float qnan = __int_as_float(0x7fffffff);
+  const float pinf = __int_as_float(0x7f800000);
   if (blk_q0 >= L1) {  // no valid query in this CTA: padding rows only
     if (lane < K)
       for (int i = 0; i < KQF; ++i) {
@@ -308,25 +328,29 @@ __global__ void __launch_bounds__(KW3 * 32)
     return;
   }
 
-  u64 QP[KQF / 2][3], THR[KQF / 2];
-  float thr[KQF], Ld[KQF];
+  u64 QQ[KQF][3], THR[KQF];
+  float cap[KQF], Ld[KQF];
   int Li[KQF];
   bool qv[KQF];
 #pragma unroll
   for (int i = 0; i < KQF; ++i) {
     qv[i] = q0 + i < L1;
-    thr[i] = qv[i] ? __int_as_float(0x7f800000) : __int_as_float(0xff800000);
-    Ld[i] = __int_as_float(0x7f800000);
+    // cap: an upper bound on the query's K-th distance, raised by one ulp so a
+    // candidate equal to it still passes (the seed is the K-th smallest distance
+    // over a subset of the targets: at least K targets lie at or below it)
+    cap[i] = pinf;
+    if (SEED && qv[i]) {
+      const float T = dists[(n * P1 + q0 + i) * K];  // written by knn_seed_kernel
+      if (T < pinf) cap[i] = __uint_as_float(__float_as_uint(T) + 1u);
+    }
+    const float th = qv[i] ? cap[i] : -pinf;
+    THR[i] = pk(th, th);
+    Ld[i] = pinf;
     Li[i] = -1;
-  }
-#pragma unroll
-  for (int ip = 0; ip < KQF / 2; ++ip) {
-    THR[ip] = pk(thr[2 * ip], thr[2 * ip + 1]);
 #pragma unroll
     for (int d = 0; d < 3; ++d) {
-      const float a = qv[2 * ip] ? p1[(n * P1 + q0 + 2 * ip) * 3 + d] : 0.f;
-      const float c = qv[2 * ip + 1] ? p1[(n * P1 + q0 + 2 * ip + 1) * 3 + d] : 0.f;
-      QP[ip][d] = pk(a, c);
+      const float a = qv[i] ? p1[(n * P1 + q0 + i) * 3 + d] : 0.f;
+      QQ[i][d] = pk(a, a);
     }
   }
   const bool any_q = q0 < L1;
@@ -337,11 +361,10 @@ __global__ void __launch_bounds__(KW3 * 32)
   }
   __syncthreads();
   // start tile t's copy into buffer t & 1: the 16-byte aligned body by one bulk
-  // copy, the rest (and NaN padding up to whole vote batches) by plain accesses
+  // copy, the rest by plain loads
   auto issue = [&](int t) {
     const int64_t t0 = (int64_t)t * KT3;
     const int nt = (int)min64(KT3, L2 - t0);
-    const int padded = (nt + KSTEP * KS - 1) / (KSTEP * KS) * (KSTEP * KS);
     const float* src = p2 + (n * P2 + t0) * 3;
     float* dst = s_raw[t & 1];
     const int nfl = nt * 3;
@@ -351,86 +374,80 @@ __global__ void __launch_bounds__(KW3 * 32)
       mbar_expect_tx(&s_bar[t & 1], (unsigned)bulk * 4u);
       if (bulk) bulk_g2s(dst, src, (unsigned)bulk * 4u, &s_bar[t & 1]);
     }
-    for (int e = bulk + threadIdx.x; e < padded * 3; e += blockDim.x) dst[e] = e < nfl ? __ldg(src + e) : qnan;
+    for (int e = bulk + threadIdx.x; e < nfl; e += blockDim.x) dst[e] = __ldg(src + e);
   };
   unsigned phase[2] = {0u, 0u};
   issue(0);
   if (ntiles > 1) issue(1);
   for (int t = 0; t < ntiles; ++t) {
     const int b = t & 1;
-    const int64_t t0 = (int64_t)t * KT3;
+    const int t0 = t * KT3;
     const int nt = (int)min64(KT3, L2 - t0);
-    const int nbat = (nt + KSTEP * KS - 1) / (KSTEP * KS);
+    const int nsteps = (nt + KP3 - 1) / KP3;
     mbar_wait(&s_bar[b], phase[b], &g_knn_device_error);
     phase[b] ^= 1u;
-    __syncthreads();  // plain-loaded elements and padding visible too
+    __syncthreads();  // tile t complete in s_raw[b]; the previous scan is done with s_soa
+    {
+      const float* raw = s_raw[b];
+      for (int e = threadIdx.x; e < nsteps * KP3; e += blockDim.x) {
+        const bool ok = e < nt;
+        s_soa[0][e] = ok ? raw[e * 3] : qnan;
+        s_soa[1][e] = ok ? raw[e * 3 + 1] : qnan;
+        s_soa[2][e] = ok ? raw[e * 3 + 2] : qnan;
+      }
+    }
+    __syncthreads();  // s_soa ready, s_raw[b] free
+    if (t + 2 < ntiles) issue(t + 2);
     if (any_q) {
-      const float* tile = s_raw[b];
 #pragma unroll 1
-      for (int bt = 0; bt < nbat; ++bt) {
-        float dv[KS][KQF];
-        u64 sg[KS][KQF / 2];
+      for (int s = 0; s < nsteps; ++s) {
+        const int e = s * KP3 + 2 * lane;
+        const u64 X = *reinterpret_cast<const u64*>(&s_soa[0][e]);
+        const u64 Y = *reinterpret_cast<const u64*>(&s_soa[1][e]);
+        const u64 Z = *reinterpret_cast<const u64*>(&s_soa[2][e]);
+        u64 dv[KQF], sg[KQF];
         unsigned acc = 0;
 #pragma unroll
-        for (int st = 0; st < KS; ++st) {
-          const float* cp = tile + ((bt * KS + st) * KSTEP + lane) * 3;
-          const float cx = cp[0], cy = cp[1], cz = cp[2];
-          const u64 CX = pk(cx, cx), CY = pk(cy, cy), CZ = pk(cz, cz);
-#pragma unroll
-          for (int ip = 0; ip < KQF / 2; ++ip) {
-            // packed fp32x2 sub/mul for two queries; scalar .rn adds (never
-            // fused): ((dx*dx + dy*dy) + dz*dz), every operation rounded
-            const u64 dx = sub2(QP[ip][0], CX), dy = sub2(QP[ip][1], CY), dz = sub2(QP[ip][2], CZ);
-            float x0, x1, y0, y1, z0, z1;
-            upk(mul2(dx, dx), x0, x1);
-            upk(mul2(dy, dy), y0, y1);
-            upk(mul2(dz, dz), z0, z1);
-            dv[st][2 * ip] = __fadd_rn(__fadd_rn(x0, y0), z0);
-            dv[st][2 * ip + 1] = __fadd_rn(__fadd_rn(x1, y1), z1);
-            sg[st][ip] = sub2(pk(dv[st][2 * ip], dv[st][2 * ip + 1]), THR[ip]);
-            acc |= (unsigned)sg[st][ip] | (unsigned)(sg[st][ip] >> 32);
-          }
+        for (int i = 0; i < KQF; ++i) {
+          const u64 dx = sub2(QQ[i][0], X), dy = sub2(QQ[i][1], Y), dz = sub2(QQ[i][2], Z);
+          float x0, x1, y0, y1, z0, z1;
+          upk(mul2(dx, dx), x0, x1);
+          upk(mul2(dy, dy), y0, y1);
+          upk(mul2(dz, dz), z0, z1);
+          dv[i] = pk(__fadd_rn(__fadd_rn(x0, y0), z0), __fadd_rn(__fadd_rn(x1, y1), z1));
+          sg[i] = sub2(dv[i], THR[i]);
+          acc |= (unsigned)sg[i] | (unsigned)(sg[i] >> 32);
         }
         if (__any_sync(0xffffffffu, (int)acc < 0)) {
+          const int cbase = t0 + s * KP3;
+          // the lane's pass bits (two per query, from the sign bits) and, by one
+          // redux, the warp's set of queries with candidates
+          unsigned m = 0;
 #pragma unroll
-          for (int st = 0; st < KS; ++st) {
-            const int cbase = (int)t0 + (bt * KS + st) * KSTEP;
-            // this lane's pass bits (one per query, from the sign bits) and,
-            // by one redux, the warp's set of queries with candidates
-            unsigned m = 0;
+          for (int i = 0; i < KQF; ++i)
+            m |= (((unsigned)sg[i] >> 31) | (((unsigned)(sg[i] >> 32) >> 31) << 1)) << (2 * i);
+          const unsigned qm = __reduce_or_sync(0xffffffffu, m);
 #pragma unroll
-            for (int ip = 0; ip < KQF / 2; ++ip)
-              m |= (((unsigned)sg[st][ip] >> 31) | (((unsigned)(sg[st][ip] >> 32) >> 31) << 1)) << (2 * ip);
-            const unsigned qm = __reduce_or_sync(0xffffffffu, m);
-#pragma unroll
-            for (int i = 0; i < KQF; ++i) {
-              if (!((qm >> i) & 1u)) continue;
-              unsigned bal = __ballot_sync(0xffffffffu, (m >> i) & 1u);
-              while (bal) {
-                const int src = __ffs(bal) - 1;
-                bal &= bal - 1;
-                // the list spans all 32 lanes: a candidate that passed the
-                // (possibly stale) filter but not the current K-th entry lands
-                // in a lane >= K and never reaches the output, so no per-
-                // candidate threshold re-check is needed
-                const float cd = __shfl_sync(0xffffffffu, dv[st][i], src);
-                const float upd = __shfl_up_sync(0xffffffffu, Ld[i], 1);
-                const int upi = __shfl_up_sync(0xffffffffu, Li[i], 1);
-                if (cd < Ld[i]) {
-                  const bool take_prev = lane > 0 && cd < upd;
-                  Ld[i] = take_prev ? upd : cd;
-                  Li[i] = take_prev ? upi : cbase + src;
-                }
-              }
-              thr[i] = __shfl_sync(0xffffffffu, Ld[i], K - 1);
-              THR[i >> 1] = pk(thr[i & ~1], thr[i | 1]);
+          for (int i = 0; i < KQF; ++i) {
+            if (!((qm >> (2 * i)) & 3u)) continue;
+            const unsigned mine = (m >> (2 * i)) & 3u;
+            unsigned bal = __ballot_sync(0xffffffffu, mine != 0u);
+            float va, vb;
+            upk(dv[i], va, vb);
+            while (bal) {
+              const int src = __ffs(bal) - 1;
+              bal &= bal - 1;
+              const unsigned pb = __shfl_sync(0xffffffffu, mine, src);
+              if (pb & 1u) knn_list_insert(Ld[i], Li[i], __shfl_sync(0xffffffffu, va, src), cbase + 2 * src, lane);
+              if (pb & 2u) knn_list_insert(Ld[i], Li[i], __shfl_sync(0xffffffffu, vb, src), cbase + 2 * src + 1, lane);
             }
+            float th = __shfl_sync(0xffffffffu, Ld[i], K - 1);
+            if constexpr (SEED) th = fminf(th, cap[i]);
+            THR[i] = pk(th, th);
           }
         }
       }
     }
-    __syncthreads();  // buffer b free
-    if (t + 2 < ntiles) issue(t + 2);
   }
   if (lane < K) {
 #pragma unroll
@@ -445,11 +462,304 @@ __global__ void __launch_bounds__(KW3 * 32)
   }
 }
 
+// ---- threshold seeds for the fp32 D=3 kernel ----
+// The scan of the kernel above accepts a candidate whenever it beats the K-th
+// entry of the query's list so far; over targets in index order that is about
+// K(1 + ln(L2/K)) insertions per query (~110 for config 4), and the insertions,
+// not the distances, dominate the kernel's instructions.  A seed T -- the K-th
+// smallest distance of the query to some subset of the targets, computed with
+// the kernel's own arithmetic -- is an upper bound on the true K-th distance,
+// so capping the threshold at T from the start changes no result (every target
+// of the final list lies at or below T) but rejects almost every candidate that
+// would be evicted later.  The subset is the 128 targets around the query's
+// position in a Morton order of the targets (a counting sort over 16^3 cells of
+// the batch's bounding box), and T is the K-th smallest of the 32 lane minima of
+// those 128 distances (K <= 32 lanes each holding a distinct target): ~30
+// accepted candidates per query on uniform clouds instead of ~110.  The scan
+// order, the acceptance rule and the output are unchanged.
+constexpr int KC_AXIS_BITS = 4;
+constexpr int KC_CELLS = 1 << (3 * KC_AXIS_BITS);  // 4096 Morton cells
+constexpr int KC_THREADS = 1024;
+constexpr int KC_PPT = 8;        // targets per thread held in registers (larger clouds loop)
+constexpr int KSD_WINDOW = 128;  // targets per seed window (4 per lane)
+constexpr int KSD_WARPS = 8;
+constexpr int KSD_QPW = 4;  // queries per warp, processed together
+constexpr int KSD_QPB = KSD_WARPS * KSD_QPW;
+constexpr int64_t kSeedMinTargets = 1024;  // below this the plain scan is short anyway
+
+struct KnnCells {
+  float* hdr;    // per batch: lo[3], inv[3] (cell = (x - lo) * inv), 8 floats
+  int* cstart;   // per batch: KC_CELLS + 1 cell starts into `order`
+  void* order;   // per batch, the L2 valid targets in cell order: float4 {x, y, z, 0}
+                 // copies (COORDS) or int32 indices (when the copies do not fit)
+};
+
+static size_t align16(size_t v) { return (v + 15) & ~(size_t)15; }
+
+static size_t knn_seed_scratch_bytes(int64_t N, int64_t P2, bool coords) {
+  return align16((size_t)N * 8 * sizeof(float)) + align16((size_t)N * (KC_CELLS + 1) * sizeof(int)) +
+         (size_t)N * P2 * (coords ? sizeof(float4) : sizeof(int));
+}
+
+static KnnCells knn_cells_layout(void* base, int64_t N) {
+  char* p = (char*)base;
+  KnnCells c;
+  c.hdr = (float*)p;
+  p += align16((size_t)N * 8 * sizeof(float));
+  c.cstart = (int*)p;
+  p += align16((size_t)N * (KC_CELLS + 1) * sizeof(int));
+  c.order = p;
+  return c;
+}
+
+static bool knn_seed_enabled() {
+  static const int on = [] {
+    const char* e = getenv("TPO_KNN_SEED");
+    return (e && e[0] == '0') ? 0 : 1;
+  }();
+  return on != 0;
+}
+
+__device__ __forceinline__ unsigned kc_spread4(unsigned v) {
+  return (v & 1u) | ((v & 2u) << 2) | ((v & 4u) << 4) | ((v & 8u) << 6);
+}
+
+__device__ __forceinline__ int kc_cell(float x, float y, float z, const float* h) {
+  const float lim = (float)((1 << KC_AXIS_BITS) - 1);
+  const unsigned cx = (unsigned)fminf(fmaxf((x - h[0]) * h[3], 0.f), lim);
+  const unsigned cy = (unsigned)fminf(fmaxf((y - h[1]) * h[4], 0.f), lim);
+  const unsigned cz = (unsigned)fminf(fmaxf((z - h[2]) * h[5], 0.f), lim);
+  return (int)(kc_spread4(cx) | (kc_spread4(cy) << 1) | (kc_spread4(cz) << 2));
+}
+
+// One CTA per batch: bounding box, cell histogram, scan, scatter of the target
+// indices.  Up to KC_THREADS * KC_PPT targets stay in registers between the
+// passes (one round of loads); larger clouds re-read them.
+template <bool COORDS>
+__global__ void __launch_bounds__(KC_THREADS)
+    knn_cells_kernel(const float* __restrict__ p2, const int64_t* __restrict__ len2, int64_t N,
+                     int64_t P2, float* __restrict__ hdr, int* __restrict__ cstart,
+                     void* __restrict__ order) {
+  __shared__ int s_cnt[KC_CELLS];
+  __shared__ float s_red[6][KC_THREADS / 32];
+  __shared__ int s_wsum[KC_THREADS / 32];
+  __shared__ float s_h[6];
+  const int64_t n = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int L2 = (int)(len2 ? min64(max64(len2[n], 0), P2) : P2);
+  const float* src = p2 + n * P2 * 3;
+  const bool regs = L2 <= KC_THREADS * KC_PPT;
+  const float pinf = __int_as_float(0x7f800000);
+  float px[KC_PPT], py[KC_PPT], pz[KC_PPT];
+  float mn[3] = {pinf, pinf, pinf};
+  float mx[3] = {-pinf, -pinf, -pinf};
+  auto fold = [&](float x, float y, float z) {
+    mn[0] = fminf(mn[0], x); mx[0] = fmaxf(mx[0], x);
+    mn[1] = fminf(mn[1], y); mx[1] = fmaxf(mx[1], y);
+    mn[2] = fminf(mn[2], z); mx[2] = fmaxf(mx[2], z);
+  };
+  if (regs) {
+#pragma unroll
+    for (int j = 0; j < KC_PPT; ++j) {
+      const int i = tid + j * KC_THREADS;
+      const bool ok = i < L2;
+      px[j] = ok ? src[i * 3] : 0.f;
+      py[j] = ok ? src[i * 3 + 1] : 0.f;
+      pz[j] = ok ? src[i * 3 + 2] : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < KC_PPT; ++j)
+      if (tid + j * KC_THREADS < L2) fold(px[j], py[j], pz[j]);
+  } else {
+    for (int i = tid; i < L2; i += KC_THREADS) fold(src[i * 3], src[i * 3 + 1], src[i * 3 + 2]);
+  }
+#pragma unroll
+  for (int d = 0; d < 3; ++d)
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      mn[d] = fminf(mn[d], __shfl_xor_sync(0xffffffffu, mn[d], o));
+      mx[d] = fmaxf(mx[d], __shfl_xor_sync(0xffffffffu, mx[d], o));
+    }
+  if (lane == 0)
+#pragma unroll
+    for (int d = 0; d < 3; ++d) {
+      s_red[d][warp] = mn[d];
+      s_red[3 + d][warp] = mx[d];
+    }
+  for (int c = tid; c < KC_CELLS; c += KC_THREADS) s_cnt[c] = 0;
+  __syncthreads();
+  if (tid < 3) {
+    float lo = s_red[tid][0], hi = s_red[3 + tid][0];
+    for (int w = 1; w < KC_THREADS / 32; ++w) {
+      lo = fminf(lo, s_red[tid][w]);
+      hi = fmaxf(hi, s_red[3 + tid][w]);
+    }
+    const float ext = hi - lo;
+    // cells per axis / extent; 0 for a flat (or empty / non-finite) axis
+    const float inv = (ext > 0.f && ext < pinf) ? (float)(1 << KC_AXIS_BITS) / ext : 0.f;
+    s_h[tid] = (lo > -pinf && lo < pinf) ? lo : 0.f;
+    s_h[3 + tid] = inv;
+  }
+  __syncthreads();
+  int cell[KC_PPT];
+  if (regs) {
+#pragma unroll
+    for (int j = 0; j < KC_PPT; ++j) {
+      cell[j] = kc_cell(px[j], py[j], pz[j], s_h);
+      if (tid + j * KC_THREADS < L2) atomicAdd(&s_cnt[cell[j]], 1);
+    }
+  } else {
+    for (int i = tid; i < L2; i += KC_THREADS)
+      atomicAdd(&s_cnt[kc_cell(src[i * 3], src[i * 3 + 1], src[i * 3 + 2], s_h)], 1);
+  }
+  __syncthreads();
+  // exclusive scan of the 4096 counts: 4 per thread, then over the block
+  constexpr int PER = KC_CELLS / KC_THREADS;
+  int v[PER], sum = 0;
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    v[j] = s_cnt[tid * PER + j];
+    sum += v[j];
+  }
+  int incl = sum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  if (lane == 31) s_wsum[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int w = s_wsum[lane];
+    int wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += t;
+    }
+    s_wsum[lane] = wi - w;
+  }
+  __syncthreads();
+  int run = s_wsum[warp] + incl - sum;
+  int* cs = cstart + n * (KC_CELLS + 1);
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    cs[tid * PER + j] = run;
+    s_cnt[tid * PER + j] = run;  // becomes the scatter cursor
+    run += v[j];
+  }
+  if (tid == 0) {
+    cs[KC_CELLS] = L2;
+#pragma unroll
+    for (int d = 0; d < 6; ++d) hdr[n * 8 + d] = s_h[d];
+  }
+  __syncthreads();
+  auto put = [&](int pos, int i, float x, float y, float z) {
+    if constexpr (COORDS) ((float4*)order)[n * P2 + pos] = make_float4(x, y, z, 0.f);
+    else ((int*)order)[n * P2 + pos] = i;
+  };
+  if (regs) {
+#pragma unroll
+    for (int j = 0; j < KC_PPT; ++j) {
+      const int i = tid + j * KC_THREADS;
+      if (i < L2) put(atomicAdd(&s_cnt[cell[j]], 1), i, px[j], py[j], pz[j]);
+    }
+  } else {
+    for (int i = tid; i < L2; i += KC_THREADS) {
+      const float x = src[i * 3], y = src[i * 3 + 1], z = src[i * 3 + 2];
+      put(atomicAdd(&s_cnt[kc_cell(x, y, z, s_h)], 1), i, x, y, z);
+    }
+  }
+}
+
+// One warp per KSD_QPW queries, processed together so that their loads and
+// shuffle chains overlap: the seed T (see above) into dists[row, 0].
+template <bool COORDS>
+__global__ void __launch_bounds__(KSD_WARPS * 32)
+    knn_seed_kernel(const float* __restrict__ p1, const float* __restrict__ p2,
+                    const int64_t* __restrict__ len1, const int64_t* __restrict__ len2, int64_t N,
+                    int64_t P1, int64_t P2, int K, int sblocks, const float* __restrict__ hdr,
+                    const int* __restrict__ cstart, const void* __restrict__ order,
+                    float* __restrict__ seeds) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t n = blockIdx.x / sblocks;
+  const int64_t qb = (int64_t)(blockIdx.x % sblocks) * KSD_QPB + warp * KSD_QPW;
+  const int64_t L1 = len1 ? min64(max64(len1[n], 0), P1) : P1;
+  if (qb >= L1) return;
+  const int L2 = (int)(len2 ? min64(max64(len2[n], 0), P2) : P2);
+  const float* h = hdr + n * 8;
+  const int* cs = cstart + n * (KC_CELLS + 1);
+  const int* od = (const int*)order + n * P2;
+  const float4* oc = (const float4*)order + n * P2;
+  const float* tp = p2 + n * P2 * 3;
+  constexpr int J = KSD_WINDOW / 32;
+  float qx[KSD_QPW], qy[KSD_QPW], qz[KSD_QPW], m[KSD_QPW];
+  int a[KSD_QPW];
+  float4 tc[KSD_QPW][J];
+#pragma unroll
+  for (int u = 0; u < KSD_QPW; ++u) {
+    const int64_t q = min64(qb + u, L1 - 1);  // past L1: a duplicate, not stored
+    qx[u] = p1[(n * P1 + q) * 3];
+    qy[u] = p1[(n * P1 + q) * 3 + 1];
+    qz[u] = p1[(n * P1 + q) * 3 + 2];
+  }
+#pragma unroll
+  for (int u = 0; u < KSD_QPW; ++u) {
+    const int c = kc_cell(qx[u], qy[u], qz[u], h);
+    const int mid = (cs[c] + cs[c + 1]) >> 1;
+    a[u] = max(0, min(mid - KSD_WINDOW / 2, L2 - KSD_WINDOW));
+  }
+  // the window's targets (NaN past L2: a NaN distance never wins a min)
+  const float qnan = __int_as_float(0x7fffffff);
+#pragma unroll
+  for (int u = 0; u < KSD_QPW; ++u)
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      const int t = a[u] + j * 32 + lane;
+      if (t >= L2) {
+        tc[u][j] = make_float4(qnan, qnan, qnan, 0.f);
+      } else if constexpr (COORDS) {
+        tc[u][j] = oc[t];
+      } else {
+        const float* c = tp + (int64_t)od[t] * 3;
+        tc[u][j] = make_float4(c[0], c[1], c[2], 0.f);
+      }
+    }
+#pragma unroll
+  for (int u = 0; u < KSD_QPW; ++u) {
+    m[u] = __int_as_float(0x7f800000);
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      // the fp32 D=3 kernel's arithmetic: ((dx*dx + dy*dy) + dz*dz), dx = q - t,
+      // every operation rounded
+      const float4 c = tc[u][j];
+      const float dx = __fsub_rn(qx[u], c.x), dy = __fsub_rn(qy[u], c.y), dz = __fsub_rn(qz[u], c.z);
+      const float d = __fadd_rn(__fadd_rn(__fmul_rn(dx, dx), __fmul_rn(dy, dy)), __fmul_rn(dz, dz));
+      m[u] = fminf(m[u], d);
+    }
+  }
+  // K-th smallest of the 32 lane minima (each lane's targets are distinct):
+  // bitonic sort over the warp
+#pragma unroll
+  for (int k = 2; k <= 32; k <<= 1)
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      const bool lo = ((lane & j) == 0) == ((lane & k) == 0);
+#pragma unroll
+      for (int u = 0; u < KSD_QPW; ++u) {
+        const float p = __shfl_xor_sync(0xffffffffu, m[u], j);
+        m[u] = lo ? fminf(m[u], p) : fmaxf(m[u], p);
+      }
+    }
+#pragma unroll
+  for (int u = 0; u < KSD_QPW; ++u) {
+    const float T = __shfl_sync(0xffffffffu, m[u], K - 1);
+    if (lane == 0 && qb + u < L1) seeds[(n * P1 + qb + u) * K] = T;
+  }
+}
+
 #ifndef TPO_KQF
 #define TPO_KQF 4
-#endif
-#ifndef TPO_KS
-#define TPO_KS 1
 #endif
 
 template <int Q>
@@ -459,8 +769,34 @@ static int launch_knn_f32x3_q(const float* p1, const float* p2, const int64_t* l
   const int qblocks = (int)((P1 + KW3 * Q - 1) / (KW3 * Q));
   const int64_t ctas = N * qblocks;
   if (ctas <= 0) return TPO_OK;
-  knn_fwd_f32x3_kernel<Q, TPO_KS><<<(unsigned)ctas, KW3 * 32, 0, st>>>(p1, p2, l1, l2, N, P1, P2, K,
-                                                                     qblocks, dists, idxs);
+  const size_t room = (size_t)N * P1 * K * sizeof(int64_t);
+  const bool coords = room >= knn_seed_scratch_bytes(N, P2, true);
+  const bool seed = knn_seed_enabled() && P2 >= kSeedMinTargets &&
+                    (coords || room >= knn_seed_scratch_bytes(N, P2, false));
+  if (seed) {
+    // the cell order of the targets lives in the idxs buffer until the main
+    // kernel overwrites it; the seeds in dists[row, 0]
+    const KnnCells c = knn_cells_layout(idxs, N);
+    if (coords)
+      knn_cells_kernel<true><<<(unsigned)N, KC_THREADS, 0, st>>>(p2, l2, N, P2, c.hdr, c.cstart, c.order);
+    else
+      knn_cells_kernel<false><<<(unsigned)N, KC_THREADS, 0, st>>>(p2, l2, N, P2, c.hdr, c.cstart, c.order);
+    int s = check_launch();
+    if (s) return s;
+    const int64_t sblocks = (P1 + KSD_QPB - 1) / KSD_QPB;
+    if (coords)
+      knn_seed_kernel<true><<<(unsigned)(N * sblocks), KSD_WARPS * 32, 0, st>>>(
+          p1, p2, l1, l2, N, P1, P2, K, (int)sblocks, c.hdr, c.cstart, c.order, dists);
+    else
+      knn_seed_kernel<false><<<(unsigned)(N * sblocks), KSD_WARPS * 32, 0, st>>>(
+          p1, p2, l1, l2, N, P1, P2, K, (int)sblocks, c.hdr, c.cstart, c.order, dists);
+    if ((s = check_launch())) return s;
+    knn_fwd_f32x3_kernel<Q, true><<<(unsigned)ctas, KW3 * 32, 0, st>>>(
+        p1, p2, l1, l2, N, P1, P2, K, qblocks, dists, idxs);
+  } else {
+    knn_fwd_f32x3_kernel<Q, false><<<(unsigned)ctas, KW3 * 32, 0, st>>>(
+        p1, p2, l1, l2, N, P1, P2, K, qblocks, dists, idxs);
+  }
   return check_launch();
 }
 
