@@ -767,11 +767,33 @@ __device__ __forceinline__ int32_t find_in_chunk(const T* q, const T* cloud, int
                                                  int64_t end, typename FinTraits<T>::K key,
                                                  T* xyz = nullptr) {
   T c[CH][3];
+  bool loaded = false;
+  if constexpr (std::is_same<T, float>::value && CH % 4 == 0) {
+    // a whole chunk whose start is 16-byte aligned (chunk starts are multiples
+    // of 8 columns, so this holds whenever the cloud itself is aligned): CH*3
+    // consecutive floats as float4 loads instead of CH*3 scalar ones
+    const float* src = cloud + base * 3;
+    if (base + CH <= end && ((uintptr_t)src & 15) == 0) {
+      float f[CH * 3];
 #pragma unroll
-  for (int k = 0; k < CH; ++k) {
-    const bool ok = base + k < end;
+      for (int v = 0; v < CH * 3 / 4; ++v) {
+        const float4 w = __ldg(reinterpret_cast<const float4*>(src) + v);
+        f[4 * v] = w.x; f[4 * v + 1] = w.y; f[4 * v + 2] = w.z; f[4 * v + 3] = w.w;
+      }
 #pragma unroll
-    for (int d = 0; d < 3; ++d) c[k][d] = ok ? cloud[(base + k) * 3 + d] : q[d];
+      for (int k = 0; k < CH; ++k)
+#pragma unroll
+        for (int d = 0; d < 3; ++d) c[k][d] = f[k * 3 + d];
+      loaded = true;
+    }
+  }
+  if (!loaded) {
+#pragma unroll
+    for (int k = 0; k < CH; ++k) {
+      const bool ok = base + k < end;
+#pragma unroll
+      for (int d = 0; d < 3; ++d) c[k][d] = ok ? cloud[(base + k) * 3 + d] : q[d];
+    }
   }
   int found = -1;
 #pragma unroll
