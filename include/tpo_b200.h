@@ -184,7 +184,13 @@ TPO_API int tpo_chamfer_loss_bwd_workspace(int dtype, int flags, const void* xyz
  * the first lengths2[n] points, ascending by (dist, idx).  Slots k >= lengths2[n]
  * and rows p >= lengths1[n] hold idx -1 / dist 0 (the reference CPU padding,
  * knn.cpp:44-45).  norm: 2 = squared L2, 1 = L1.  1 <= K <= 1024 (larger K returns
- * TPO_ERR_UNSUPPORTED), any D >= 1; D <= 8 with K <= 32 takes the fast kernel. */
+ * TPO_ERR_UNSUPPORTED), any D >= 1; D <= 8 with K <= 32 takes the fast kernel.
+ * fp32, D=3, L2, P2 >= 1024: the call also uses the idxs and dists buffers as
+ * its scratch (a cell order of p2 and per-query thresholds) before the final
+ * results overwrite them, so both must be distinct, writable and not read by
+ * anyone until the call completes on `stream`; no other memory is allocated.
+ * The environment variable TPO_KNN_SEED=0 (read once) turns the threshold seeds
+ * off; results are identical either way. */
 TPO_API int tpo_knn_fwd(int dtype, int flags, const void* p1, const void* p2,
                 const int64_t* lengths1, const int64_t* lengths2, int64_t N, int64_t P1,
                 int64_t P2, int64_t D, int64_t norm, int64_t K, void* dists, int64_t* idxs,
