@@ -262,10 +262,14 @@ def step_fn(cfg, mode="single", units=None, batch_share=1.0):
 
 def launches_per_step(cfg, mode="single"):
     # chamfer: fill, keys, loss reduction (fwd), gradient scatter into the
-    # forward's zero-filled workspace (bwd); knn: knn fwd, gather fwd, gather
-    # bwd, knn bwd; fps: one sampling kernel.  Row-sharded chamfer: fill (keys
-    # init), keys, finalize, partial backward.
-    return {"chamfer": 4, "knn": 4, "fps": 1}[cfg["kind"]]
+    # forward's zero-filled workspace (bwd); knn: knn fwd (fp32 D=3 with
+    # P2 >= 1024: cell sort, seeds, scan), gather fwd, gather bwd, knn bwd;
+    # fps: one sampling kernel.  Row-sharded chamfer: fill (keys init), keys,
+    # finalize, partial backward.
+    if cfg["kind"] == "knn":
+        seeded = cfg.get("dtype", "float32") == "float32" and cfg.get("M", 0) >= 1024
+        return 6 if seeded else 4
+    return {"chamfer": 4, "fps": 1}[cfg["kind"]]
 
 
 def parity_rows(dev, ws, dtype=torch.float32):
