@@ -317,7 +317,12 @@ __global__ void __launch_bounds__(KW3 * 32)
   const int64_t L2 = len2 ? min64(max64(len2[n], 0), P2) : P2;
   const float qnan = __int_as_float(0x7fffffff);
   const float pinf = __int_as_float(0x7f800000);
+  // Seeded launches follow knn_seed_kernel with programmatic serialisation:
+  // until pdl_wait() only the inputs are read (queries, the first target
+  // tiles) -- the seeds in dists and the seed kernel's scratch in idxs are
+  // touched after it.
   if (blk_q0 >= L1) {  // no valid query in this CTA: padding rows only
+    pdl_wait();
     if (lane < K)
       for (int i = 0; i < KQF; ++i) {
         const int64_t row = q0 + i;
@@ -335,16 +340,6 @@ __global__ void __launch_bounds__(KW3 * 32)
 #pragma unroll
   for (int i = 0; i < KQF; ++i) {
     qv[i] = q0 + i < L1;
-    // cap: an upper bound on the query's K-th distance, raised by one ulp so a
-    // candidate equal to it still passes (the seed is the K-th smallest distance
-    // over a subset of the targets: at least K targets lie at or below it)
-    cap[i] = pinf;
-    if (SEED && qv[i]) {
-      const float T = dists[(n * P1 + q0 + i) * K];  // written by knn_seed_kernel
-      if (T < pinf) cap[i] = __uint_as_float(__float_as_uint(T) + 1u);
-    }
-    const float th = qv[i] ? cap[i] : -pinf;
-    THR[i] = pk(th, th);
     Ld[i] = pinf;
     Li[i] = -1;
 #pragma unroll
@@ -379,6 +374,20 @@ __global__ void __launch_bounds__(KW3 * 32)
   unsigned phase[2] = {0u, 0u};
   issue(0);
   if (ntiles > 1) issue(1);
+  pdl_wait();
+#pragma unroll
+  for (int i = 0; i < KQF; ++i) {
+    // cap: an upper bound on the query's K-th distance, raised by one ulp so a
+    // candidate equal to it still passes (the seed is the K-th smallest distance
+    // over a subset of the targets: at least K targets lie at or below it)
+    cap[i] = pinf;
+    if (SEED && qv[i]) {
+      const float T = dists[(n * P1 + q0 + i) * K];  // written by knn_seed_kernel
+      if (T < pinf) cap[i] = __uint_as_float(__float_as_uint(T) + 1u);
+    }
+    const float th = qv[i] ? cap[i] : -pinf;
+    THR[i] = pk(th, th);
+  }
   for (int t = 0; t < ntiles; ++t) {
     const int b = t & 1;
     const int t0 = t * KT3;
@@ -544,6 +553,7 @@ __global__ void __launch_bounds__(KC_THREADS)
   __shared__ float s_red[6][KC_THREADS / 32];
   __shared__ int s_wsum[KC_THREADS / 32];
   __shared__ float s_h[6];
+  pdl_trigger();  // the seed kernel may start loading its queries
   const int64_t n = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int L2 = (int)(len2 ? min64(max64(len2[n], 0), P2) : P2);
@@ -681,6 +691,7 @@ __global__ void __launch_bounds__(KSD_WARPS * 32)
                     int64_t P1, int64_t P2, int K, int sblocks, const float* __restrict__ hdr,
                     const int* __restrict__ cstart, const void* __restrict__ order,
                     float* __restrict__ seeds) {
+  pdl_trigger();  // the scan may start loading its queries and first tiles
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t n = blockIdx.x / sblocks;
   const int64_t qb = (int64_t)(blockIdx.x % sblocks) * KSD_QPB + warp * KSD_QPW;
@@ -703,6 +714,9 @@ __global__ void __launch_bounds__(KSD_WARPS * 32)
     qy[u] = p1[(n * P1 + q) * 3 + 1];
     qz[u] = p1[(n * P1 + q) * 3 + 2];
   }
+  // launched after knn_cells_kernel with programmatic serialisation: the
+  // queries above are inputs; the cell table is read after this wait
+  pdl_wait();
 #pragma unroll
   for (int u = 0; u < KSD_QPW; ++u) {
     const int c = kc_cell(qx[u], qy[u], qz[u], h);
@@ -784,15 +798,12 @@ static int launch_knn_f32x3_q(const float* p1, const float* p2, const int64_t* l
     int s = check_launch();
     if (s) return s;
     const int64_t sblocks = (P1 + KSD_QPB - 1) / KSD_QPB;
-    if (coords)
-      knn_seed_kernel<true><<<(unsigned)(N * sblocks), KSD_WARPS * 32, 0, st>>>(
-          p1, p2, l1, l2, N, P1, P2, K, (int)sblocks, c.hdr, c.cstart, c.order, dists);
-    else
-      knn_seed_kernel<false><<<(unsigned)(N * sblocks), KSD_WARPS * 32, 0, st>>>(
-          p1, p2, l1, l2, N, P1, P2, K, (int)sblocks, c.hdr, c.cstart, c.order, dists);
-    if ((s = check_launch())) return s;
-    knn_fwd_f32x3_kernel<Q, true><<<(unsigned)ctas, KW3 * 32, 0, st>>>(
-        p1, p2, l1, l2, N, P1, P2, K, qblocks, dists, idxs);
+    s = launch_pdl(coords ? knn_seed_kernel<true> : knn_seed_kernel<false>, dim3((unsigned)(N * sblocks)),
+                   dim3(KSD_WARPS * 32), 0, st, p1, p2, l1, l2, N, P1, P2, K, (int)sblocks,
+                   (const float*)c.hdr, (const int*)c.cstart, (const void*)c.order, dists);
+    if (s) return s;
+    return launch_pdl(knn_fwd_f32x3_kernel<Q, true>, dim3((unsigned)ctas), dim3(KW3 * 32), 0, st, p1, p2,
+                      l1, l2, N, P1, P2, K, qblocks, dists, idxs);
   } else {
     knn_fwd_f32x3_kernel<Q, false><<<(unsigned)ctas, KW3 * 32, 0, st>>>(
         p1, p2, l1, l2, N, P1, P2, K, qblocks, dists, idxs);
