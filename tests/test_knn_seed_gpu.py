@@ -62,3 +62,37 @@ def test_seed_k1_index_scratch():
     p1 = torch.randn(2, 4096, 3, generator=g)
     p2 = torch.randn(2, 2048, 3, generator=g)
     _run(p1, p2, torch.tensor([4096, 3000]), torch.tensor([2048, 1500]), 2, 1)
+
+
+def test_seed_on_off_identical_config4():
+    # the whole of config 4 (K=16 and K=1) with and without seeds: the seeds may
+    # only remove candidates that the final list would not keep, so every index
+    # and distance must agree; the unseeded run needs a fresh process because
+    # the library reads TPO_KNN_SEED once
+    import os
+    import subprocess
+    import sys
+
+    import datagen
+    import torch_point_ops_b200 as tpo
+
+    p1, p2, l1, l2 = [t.cuda() for t in datagen.knn_config4()]
+    here = os.path.dirname(os.path.abspath(__file__))
+    code = (
+        "import sys, torch; sys.path.insert(0, %r); sys.path.insert(0, %r)\n"
+        "import datagen, torch_point_ops_b200 as tpo\n"
+        "p1, p2, l1, l2 = [t.cuda() for t in datagen.knn_config4()]\n"
+        "out = {}\n"
+        "for K in (1, 16):\n"
+        "    out[K] = [t.cpu() for t in tpo.knn_points(p1, p2, l1, l2, K=K)[:2]]\n"
+        "torch.save(out, sys.argv[1])\n" % (here, os.path.dirname(here)))
+    import tempfile
+    with tempfile.TemporaryDirectory() as tmp:
+        path = os.path.join(tmp, "unseeded.pt")
+        env = dict(os.environ, TPO_KNN_SEED="0")
+        subprocess.run([sys.executable, "-c", code, path], env=env, check=True)
+        ref = torch.load(path)
+    for K in (1, 16):
+        idx, dist = tpo.knn_points(p1, p2, l1, l2, K=K)[:2]
+        assert torch.equal(idx.cpu(), ref[K][0])
+        assert torch.equal(dist.cpu(), ref[K][1])
